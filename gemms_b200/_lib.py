@@ -1,0 +1,118 @@
+"""ctypes binding of the C ABI in ``include/gemms_moe.h``.
+
+The shared library is ``gemms_b200/lib/libgemms_b200.so`` (built in-tree by
+``gemms_b200.build``).  There is no fallback: if the library cannot be loaded
+every operator raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+c_int32 = ctypes.c_int32
+c_void_p = ctypes.c_void_p
+c_size_t = ctypes.c_size_t
+c_float = ctypes.c_float
+
+GEMMS_INPUT_BF16 = 0
+GEMMS_INPUT_FP8 = 1
+
+EXPORTS = (
+    "gemms_moe_workspace_size",
+    "gemms_moe_fwd",
+    "gemms_route",
+    "gemms_expert_ffn_workspace_size",
+    "gemms_expert_ffn",
+    "gemms_moe_check",
+    "gemms_strerror",
+    "gemms_version",
+)
+
+
+class GemmsMoeShape(ctypes.Structure):
+    _fields_ = [
+        ("T", c_int32), ("H", c_int32), ("I", c_int32), ("E", c_int32), ("E_local", c_int32),
+        ("local_expert_offset", c_int32), ("n_group", c_int32), ("topk_group", c_int32), ("top_k", c_int32),
+        ("has_shared", c_int32), ("input_mode", c_int32), ("bias_bf16", c_int32), ("inter_planes", c_int32),
+        ("routed_scaling_factor", c_float),
+    ]
+
+
+class GemmsMoeArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", GemmsMoeShape),
+        ("routing_logits", c_void_p), ("routing_bias", c_void_p),
+        ("hidden_bf16", c_void_p), ("hidden_fp8", c_void_p), ("hidden_scale", c_void_p),
+        ("w13", c_void_p), ("w13_scale", c_void_p), ("w2", c_void_p), ("w2_scale", c_void_p),
+        ("shared_w13", c_void_p), ("shared_w13_scale", c_void_p), ("shared_w2", c_void_p),
+        ("shared_w2_scale", c_void_p),
+        ("out", c_void_p), ("topk_idx_out", c_void_p), ("topk_w_out", c_void_p), ("expert_counts_out", c_void_p),
+    ]
+
+
+class GemmsError(RuntimeError):
+    """A GEMMS_ERR_* code returned by the C ABI."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where} failed: {strerror(code)} (code {code})")
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load(auto_build: bool = True) -> ctypes.CDLL:
+    """Load (building first if needed and nvcc exists) the shared library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB
+        if not os.path.exists(path) and auto_build:
+            _build.build()
+        if not os.path.exists(path):
+            raise ImportError(f"gemms_b200 CUDA library missing: {path} (run `python -m gemms_b200.build`)")
+        L = ctypes.CDLL(path)
+        L.gemms_moe_workspace_size.argtypes = [ctypes.POINTER(GemmsMoeShape)]
+        L.gemms_moe_workspace_size.restype = c_size_t
+        L.gemms_moe_fwd.argtypes = [ctypes.POINTER(GemmsMoeArgs), c_void_p, c_size_t, c_void_p]
+        L.gemms_moe_fwd.restype = c_int32
+        L.gemms_route.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]
+        L.gemms_route.restype = c_int32
+        L.gemms_expert_ffn_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32]
+        L.gemms_expert_ffn_workspace_size.restype = c_size_t
+        L.gemms_expert_ffn.argtypes = [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                       c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_size_t, c_void_p]
+        L.gemms_expert_ffn.restype = c_int32
+        L.gemms_moe_check.argtypes = [c_void_p, c_void_p, ctypes.POINTER(c_int32)]
+        L.gemms_moe_check.restype = c_int32
+        L.gemms_strerror.argtypes = [c_int32]
+        L.gemms_strerror.restype = ctypes.c_char_p
+        L.gemms_version.argtypes = []
+        L.gemms_version.restype = ctypes.c_char_p
+        _lib = L
+        return L
+
+
+def strerror(code: int) -> str:
+    try:
+        return load(auto_build=False).gemms_strerror(code).decode()
+    except Exception:  # library itself unavailable
+        return f"error {code}"
+
+
+def check(code: int, where: str) -> None:
+    if code != 0:
+        raise GemmsError(code, where)

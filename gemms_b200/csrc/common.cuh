@@ -1,0 +1,135 @@
+// common.cuh -- shared definitions of the MoE kernels and their host launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cstdint>
+#include <cstddef>
+
+#include "../../include/gemms_moe.h"
+
+namespace gemms {
+
+constexpr int kBlock = 128;          // quantisation block (1x128 activations, 128x128 weights)
+constexpr float kFp8Max = 448.0f;    // largest finite e4m3 magnitude
+
+// Device error word bits (OR-ed by kernels, read by gemms_moe_check).
+enum : int {
+  kErrGemmProducerWait = 1 << 0,
+  kErrGemmMmaWait = 1 << 1,
+  kErrGemmEpilogueWait = 1 << 2,
+  kErrBadExpertIndex = 1 << 3,
+  kErrRowOverflow = 1 << 4,
+};
+
+#define GEMMS_CUDA_TRY(expr)                         \
+  do {                                               \
+    cudaError_t _e = (expr);                         \
+    if (_e != cudaSuccess) return GEMMS_ERR_CUDA;    \
+  } while (0)
+
+__host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- internal launchers (stream-ordered, return GEMMS_* codes) ----------
+struct RouteArgs {
+  const float* logits;
+  const void* bias;
+  int bias_bf16;
+  int T, E, n_group, topk_group, top_k;
+  float rsf;
+  int local_offset, E_local;  // histogram only counts experts in [local_offset, local_offset+E_local)
+  int32_t* topk_idx;          // [T, top_k]
+  float* topk_w;              // [T, top_k]
+  int32_t* counts;            // [E_local]
+  int32_t* pair_row;          // optional [T, top_k], set to -1 (filled later by assign)
+};
+int launch_route(const RouteArgs& a, cudaStream_t s);
+
+// Builds per-group row offsets and the 128-row M-tile list.
+// groups = E_local (+1 if a shared expert is appended with `shared_rows` rows).
+struct PlanArgs {
+  const int32_t* counts;  // [E_local]
+  int E_local;
+  int shared_rows;        // 0: no shared group
+  int32_t* offsets;       // [groups + 1]
+  int32_t* tile_group;    // [max_tiles]
+  int32_t* tile_row0;
+  int32_t* tile_rows;
+  int32_t* num_tiles;     // [1]
+  int max_tiles;
+  int* err;
+};
+int launch_plan(const PlanArgs& a, cudaStream_t s);
+
+// Deterministic (token-ordered) row assignment within each local expert.
+struct AssignArgs {
+  const int32_t* topk_idx;
+  const float* topk_w;
+  int T, top_k, local_offset, E_local;
+  const int32_t* offsets;
+  int32_t* row_token;     // [rows]
+  float* row_weight;      // [rows]
+  int32_t* pair_row;      // [T, top_k]
+  int shared_rows;        // >0: rows offsets[E_local] + t get token t, weight 1
+};
+int launch_assign(const AssignArgs& a, cudaStream_t s);
+
+// Gather (and for bf16 input, quantise per 1x128) activation rows into the
+// expert-grouped operand: rows_fp8 [R, H], rows_scale [H/128, ld].
+struct PermuteArgs {
+  int mode;                        // GEMMS_INPUT_BF16 / GEMMS_INPUT_FP8
+  const __nv_bfloat16* x_bf16;     // [T, H]
+  const uint8_t* x_fp8;            // [T, H]
+  const float* x_scale;            // [H/128, T]
+  int T, H, top_k;
+  const int32_t* pair_row;         // [T, top_k] (-1 = not local)
+  const int32_t* shared_row0;      // device int (nullptr: none); token t also goes to row *shared_row0 + t
+  uint8_t* rows_fp8;
+  float* rows_scale;
+  int scale_ld;
+};
+int launch_permute(const PermuteArgs& a, cudaStream_t s);
+
+// fp32 [n] -> bf16 [n]
+int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s);
+
+// Grouped block-scaled FP8 GEMMs.
+struct GemmGroupsArgs {
+  const int32_t* tile_group;
+  const int32_t* tile_row0;
+  const int32_t* tile_rows;
+  const int32_t* num_tiles;
+  int max_tiles;
+  int shared_group;  // group index that uses the shared expert's weights (-1: none)
+};
+
+struct Gemm1Args {
+  GemmGroupsArgs g;
+  const uint8_t* a;  int a_rows;  const float* a_scale; int a_scale_ld;    // [R, H], [H/128, ld]
+  const uint8_t* w13; const float* w13_scale; int E_local;                 // [E_local, 2I, H]
+  const uint8_t* sw13; const float* sw13_scale;                            // shared [2I, H]
+  int H, I;
+  int planes;                                                               // 2 or 3
+  uint8_t* inter; float* inter_scale; int inter_scale_ld;                   // [R, planes*I], [I/128, ld]
+  int* err;
+};
+int launch_gemm1(const Gemm1Args& a, cudaStream_t s);
+
+struct Gemm2Args {
+  GemmGroupsArgs g;
+  const uint8_t* inter; int a_rows; const float* inter_scale; int inter_scale_ld;
+  const uint8_t* w2; const float* w2_scale; int E_local;                   // [E_local, H, I]
+  const uint8_t* sw2; const float* sw2_scale;                              // shared [H, I]
+  int H, I, planes;
+  const int32_t* row_dest; const float* row_weight;                        // [R]
+  float* out;                                                               // [n_dest, H] fp32 (+=)
+  int* err;
+};
+int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
+
+int num_sms();
+
+}  // namespace gemms

@@ -1,0 +1,497 @@
+// grouped_gemm.cu -- grouped, 128x128 block-scaled FP8 GEMMs on tcgen05.
+//
+// GEMM1 (gate/up projection + SwiGLU) and GEMM2 (down projection + routing
+// weight + combine) of the MoE layer.  Reference: the per-expert loop of the
+// oracle, flashinfer_baseline.py:135-167 (G1 = A_e W13_e^T; C = silu(G1[:,I:])
+// * G1[:,:I]; O = C W2_e^T; out += w * O), and the reference's attempt at it,
+// persistent_gemm_kernel in persistent_kernel2.cu:388-890.
+//
+// Design (one persistent CTA per SM, 320 threads, warp-specialised):
+//   warp 0      TMA producer: A tile(s) [128 rows x 128 B] per plane and two
+//               128-row weight boxes per stage into a 3-4 deep smem ring.
+//   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
+//               (M=128, N=256, K=32 e4m3) from one thread; each 128-wide K
+//               block goes to one of two TMEM partial accumulators.
+//   warps 2-9   "promotion" epilogue: for every K block read the fp32 partial
+//               from TMEM, multiply by a_scale[row,kb] * w_scale[nblk,kb] and
+//               accumulate in registers (the block scales are arbitrary fp32,
+//               so the MX block-scaled MMA kinds cannot absorb them).  Then:
+//               GEMM1: SwiGLU, then re-quantise C per 1x128 into PLANES e4m3
+//                      planes sharing one scale (hi, residual, ...), so GEMM2
+//                      sums the planes in the same TMEM accumulator.
+//               GEMM2: scale by the routing weight and add the fp32 row into
+//                      the token's output row with vector atomics.
+// Work units are (M tile, N tile) with N fastest: CTAs working on adjacent
+// units share the A tile, and the M tiles of one expert are adjacent so their
+// weight tiles are read from HBM once and from L2 after that.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace gemms {
+namespace {
+using namespace sm100;
+
+constexpr int BM = 128;                 // rows per tile = TMEM lanes
+constexpr int BN = 256;                 // output columns per tile
+constexpr int BK = 128;                 // K (bytes) per stage = one scale block
+constexpr int UMMA_K = 32;              // K per tcgen05.mma for 8-bit inputs
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kTmemCols = 512;     // 2 partial accumulators x 256 columns
+constexpr int kTileA = BM * BK;         // 16 KB
+constexpr int kTileB = BN * BK;         // 32 KB
+
+template <int PLANES>
+struct Cfg {
+  static constexpr int kStageBytes = PLANES * kTileA + kTileB;
+  static constexpr int kStages = PLANES == 1 ? 4 : (PLANES == 2 ? 3 : 2);
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kRingBytes + 4096 + 1024;  // + barriers/exchange + alignment slack
+};
+
+struct GemmParams {
+  const int32_t* tile_group;
+  const int32_t* tile_row0;
+  const int32_t* tile_rows;
+  const int32_t* num_tiles;
+  int max_tiles;
+  int shared_group;
+  int n_tiles;       // N tiles per M tile
+  int kb_count;      // K blocks
+  int plane_stride;  // bytes between A planes within a row
+  int w_rows;        // weight rows per expert
+  int b_row_step;    // weight rows per N tile step
+  int b_row_hi;      // row offset of the second 128-row weight box
+  const float* a_scale;
+  int a_scale_ld;
+  const float* w_scale;   // [E, w_rows/128, kb_count]
+  const float* sw_scale;  // [w_rows/128, kb_count]
+  // GEMM1 epilogue
+  uint8_t* inter;
+  float* inter_scale;
+  int inter_scale_ld;
+  int I;
+  // GEMM2 epilogue
+  const int32_t* row_dest;
+  const float* row_weight;
+  float* out;
+  int H;
+  int* err;
+};
+
+__device__ __forceinline__ uint16_t f2_to_e4m3x2(float a, float b) {
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ float2 e4m3x2_to_f2(uint16_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Drain wait used on exit: bounded, ignores the abort flag, reports nothing.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > GEMMS_WAIT_TIMEOUT_NS) return;
+}
+
+template <int MODE, int PLANES, int OUT_PLANES>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmBs, const GemmParams p) {
+  using C = Cfg<PLANES>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kRingBytes);
+  uint64_t* empty = full + S;
+  uint64_t* pfull = empty + S;
+  uint64_t* pempty = pfull + 2;
+  uint64_t* mma_done = pempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* amax_x = reinterpret_cast<float*>(smem + C::kRingBytes + 512);  // [2 units][2 halves][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmBs);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int num_tiles = min(*p.num_tiles, p.max_tiles);
+  const int total = num_tiles * p.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int it = 0;
+      for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
+        const bool sh = (g == p.shared_group);
+        const CUtensorMap* mb = sh ? &tmBs : &tmB;
+        const int wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
+        bool ok = true;
+        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+#pragma unroll
+          for (int pl = 0; pl < PLANES; ++pl)
+            tma_load_2d(st + pl * kTileA, &tmA, &full[s], pl * p.plane_stride + kb * BK, row0, pol_a);
+          uint8_t* sb = st + PLANES * kTileA;
+          tma_load_2d(sb, mb, &full[s], kb * BK, wrow, pol_w);
+          tma_load_2d(sb + kTileA, mb, &full[s], kb * BK, wrow + p.b_row_hi, pol_w);
+        }
+        if (!ok) break;
+      }
+      // Let every copy this thread issued land before the CTA can exit.
+      for (int s = 0; s < S && s < it; ++s) {
+        const int last = s + S * ((it - 1 - s) / S);
+        mbar_wait_drain(&full[s], (last / S) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+      int it = 0, acc_it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        for (int kb = 0; kb < p.kb_count; ++kb, ++it, ++acc_it) {
+          const int buf = acc_it & 1;
+          if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, p.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + buf * BN;
+          uint8_t* st = smem + s * C::kStageBytes;
+          const uint32_t b_addr = smem_u32(st + PLANES * kTileA);
+#pragma unroll
+          for (int pl = 0; pl < PLANES; ++pl) {
+            const uint32_t a_addr = smem_u32(st + pl * kTileA);
+#pragma unroll
+            for (int ks = 0; ks < BK / UMMA_K; ++ks)
+              umma_f8f6f4(d, smem_desc_k_sw128(a_addr + ks * UMMA_K), smem_desc_k_sw128(b_addr + ks * UMMA_K),
+                          idesc, (pl | ks) != 0);
+          }
+          umma_commit(&empty[s]);
+          umma_commit(&pfull[buf]);
+        }
+      }
+      // On every exit path, wait (bounded) for this thread's MMAs to finish
+      // before the CTA can free TMEM.
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;         // TMEM lane quadrant this warp may access
+    const int h = ew >> 2;          // column half
+    const int r = q * 32 + lane;    // row within the tile
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const int wblk = p.w_rows / kBlock;
+    int acc_it = 0, unit_i = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++unit_i) {
+      const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+      const int g = p.tile_group[mt], row0 = p.tile_row0[mt], rows = p.tile_rows[mt];
+      const bool valid = r < rows;
+      const float* ws = (g == p.shared_group) ? p.sw_scale : p.w_scale + (size_t)g * wblk * p.kb_count;
+      // weight-scale rows used by this thread's two column groups
+      int blk0, blk1;
+      if (MODE == 0) {
+        blk0 = nt;                          // gate rows  [nt*128, +128)
+        blk1 = p.I / kBlock + nt;           // up rows    [I + nt*128, +128)
+      } else {
+        blk0 = blk1 = 2 * nt + h;           // output columns [nt*256 + 128h, +128)
+      }
+      const float* a_sc = p.a_scale + row0 + r;
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      float as_n = valid ? __ldg(a_sc) : 0.f;
+      float w0_n = __ldg(ws + (size_t)blk0 * p.kb_count);
+      float w1_n = __ldg(ws + (size_t)blk1 * p.kb_count);
+      for (int kb = 0; kb < p.kb_count; ++kb, ++acc_it) {
+        const float f0 = as_n * w0_n, f1 = as_n * w1_n;
+        if (kb + 1 < p.kb_count) {  // prefetch next block's scales
+          as_n = valid ? __ldg(a_sc + (size_t)(kb + 1) * p.a_scale_ld) : 0.f;
+          w0_n = __ldg(ws + (size_t)blk0 * p.kb_count + kb + 1);
+          w1_n = __ldg(ws + (size_t)blk1 * p.kb_count + kb + 1);
+        }
+        const int buf = acc_it & 1;
+        if (!mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          int col;
+          float f;
+          if (MODE == 0) {
+            col = (c < 2) ? (64 * h + 32 * c) : (128 + 64 * h + 32 * (c - 2));
+            f = (c < 2) ? f0 : f1;
+          } else {
+            col = 128 * h + 32 * c;
+            f = f0;
+          }
+          float v[32];
+          tmem_ld_32x32b_x32(lane_base + buf * BN + col, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[32 * c + i] = fmaf(f, v[i], acc[32 * c + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[buf]);
+      }
+      if (!ok) break;
+
+      if (MODE == 0) {
+        // SwiGLU: C = silu(up) * gate  (flashinfer_baseline.py:157-160)
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float up = acc[64 + j];
+          const float cval = __fdiv_rn(up, 1.0f + expf(-up)) * acc[j];
+          acc[j] = cval;
+          amax = fmaxf(amax, fabsf(cval));
+        }
+        float* ax = amax_x + (unit_i & 1) * 256;
+        ax[h * 128 + r] = amax;
+        named_bar_sync(1, kEpiWarps * 32);
+        amax = fmaxf(amax, ax[(1 - h) * 128 + r]);
+        const float scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+        if (valid) {
+          const size_t row_bytes = (size_t)OUT_PLANES * p.I;
+          uint8_t* dst = p.inter + (size_t)(row0 + r) * row_bytes + (size_t)nt * kBlock + 64 * h;
+#pragma unroll
+          for (int j0 = 0; j0 < 64; j0 += 16) {
+            uint32_t w[OUT_PLANES][4];
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              float x0 = __fdiv_rn(acc[j0 + j], scale), x1 = __fdiv_rn(acc[j0 + j + 1], scale);
+#pragma unroll
+              for (int pl = 0; pl < OUT_PLANES; ++pl) {
+                const uint16_t b2 = f2_to_e4m3x2(x0, x1);
+                if ((j & 2) == 0)
+                  w[pl][j >> 2] = b2;
+                else
+                  w[pl][j >> 2] |= static_cast<uint32_t>(b2) << 16;
+                if (pl + 1 < OUT_PLANES) {
+                  const float2 back = e4m3x2_to_f2(b2);
+                  x0 -= back.x;
+                  x1 -= back.y;
+                }
+              }
+            }
+#pragma unroll
+            for (int pl = 0; pl < OUT_PLANES; ++pl)
+              *reinterpret_cast<uint4*>(dst + (size_t)pl * p.I + j0) = make_uint4(w[pl][0], w[pl][1], w[pl][2], w[pl][3]);
+          }
+          if (h == 0) p.inter_scale[(size_t)nt * p.inter_scale_ld + row0 + r] = scale;
+        }
+      } else {
+        if (valid) {
+          const int dst = p.row_dest[row0 + r];
+          const float wgt = p.row_weight[row0 + r];
+          float* o = p.out + (size_t)dst * p.H + (size_t)nt * BN + 128 * h;
+#pragma unroll
+          for (int c = 0; c < 128; c += 4)
+            atomicAdd(reinterpret_cast<float4*>(o + c),
+                      make_float4(wgt * acc[c], wgt * acc[c + 1], wgt * acc[c + 2], wgt * acc[c + 3]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor [rows, inner] with a 128x128 box and 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride) {
+  auto fn = encode_fn();
+  if (!fn) return GEMMS_ERR_DRIVER;
+  if (!aligned16(base) || (row_stride % 16) || inner % BK) return GEMMS_ERR_ALIGN;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(BM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GEMMS_OK : GEMMS_ERR_DRIVER;
+}
+
+template <int MODE, int PLANES, int OUT_PLANES>
+int launch_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& bs, const GemmParams& p,
+                  int max_units, cudaStream_t s) {
+  auto kern = grouped_gemm_kernel<MODE, PLANES, OUT_PLANES>;
+  constexpr int smem = Cfg<PLANES>::kSmemBytes;
+  static bool attr_set = false;  // per template instance; the attribute is per device function
+  if (!attr_set) {
+    GEMMS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  const int grid = std::max(1, std::min(num_sms(), max_units));
+  kern<<<grid, kThreads, smem, s>>>(a, b, bs, p);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+}  // namespace
+
+int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
+  if (a.H % BK || a.I % BK) return GEMMS_ERR_SHAPE;
+  if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
+  CUtensorMap ma, mb, mbs;
+  int rc;
+  if ((rc = make_map(&ma, a.a, a.H, a.a_rows, a.H))) return rc;
+  if ((rc = make_map(&mb, a.w13, a.H, (uint64_t)a.E_local * 2 * a.I, a.H))) return rc;
+  if (a.sw13) {
+    if ((rc = make_map(&mbs, a.sw13, a.H, 2ull * a.I, a.H))) return rc;
+  } else {
+    mbs = mb;
+  }
+  GemmParams p{};
+  p.tile_group = a.g.tile_group;
+  p.tile_row0 = a.g.tile_row0;
+  p.tile_rows = a.g.tile_rows;
+  p.num_tiles = a.g.num_tiles;
+  p.max_tiles = a.g.max_tiles;
+  p.shared_group = a.sw13 ? a.g.shared_group : -1;
+  p.n_tiles = a.I / kBlock;
+  p.kb_count = a.H / BK;
+  p.plane_stride = 0;
+  p.w_rows = 2 * a.I;
+  p.b_row_step = kBlock;
+  p.b_row_hi = a.I;
+  p.a_scale = a.a_scale;
+  p.a_scale_ld = a.a_scale_ld;
+  p.w_scale = a.w13_scale;
+  p.sw_scale = a.sw13_scale;
+  p.inter = a.inter;
+  p.inter_scale = a.inter_scale;
+  p.inter_scale_ld = a.inter_scale_ld;
+  p.I = a.I;
+  p.H = a.H;
+  p.err = a.err;
+  const int max_units = a.g.max_tiles * p.n_tiles;
+  if (a.planes == 2) return launch_kernel<0, 1, 2>(ma, mb, mbs, p, max_units, s);
+  return launch_kernel<0, 1, 3>(ma, mb, mbs, p, max_units, s);
+}
+
+int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
+  if (a.H % BN || a.I % BK) return GEMMS_ERR_SHAPE;
+  if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
+  CUtensorMap ma, mb, mbs;
+  int rc;
+  if ((rc = make_map(&ma, a.inter, (uint64_t)a.planes * a.I, a.a_rows, (uint64_t)a.planes * a.I))) return rc;
+  if ((rc = make_map(&mb, a.w2, a.I, (uint64_t)a.E_local * a.H, a.I))) return rc;
+  if (a.sw2) {
+    if ((rc = make_map(&mbs, a.sw2, a.I, (uint64_t)a.H, a.I))) return rc;
+  } else {
+    mbs = mb;
+  }
+  GemmParams p{};
+  p.tile_group = a.g.tile_group;
+  p.tile_row0 = a.g.tile_row0;
+  p.tile_rows = a.g.tile_rows;
+  p.num_tiles = a.g.num_tiles;
+  p.max_tiles = a.g.max_tiles;
+  p.shared_group = a.sw2 ? a.g.shared_group : -1;
+  p.n_tiles = a.H / BN;
+  p.kb_count = a.I / BK;
+  p.plane_stride = a.I;
+  p.w_rows = a.H;
+  p.b_row_step = BN;
+  p.b_row_hi = kBlock;
+  p.a_scale = a.inter_scale;
+  p.a_scale_ld = a.inter_scale_ld;
+  p.w_scale = a.w2_scale;
+  p.sw_scale = a.sw2_scale;
+  p.row_dest = a.row_dest;
+  p.row_weight = a.row_weight;
+  p.out = a.out;
+  p.H = a.H;
+  p.I = a.I;
+  p.err = a.err;
+  const int max_units = a.g.max_tiles * p.n_tiles;
+  if (a.planes == 2) return launch_kernel<1, 2, 1>(ma, mb, mbs, p, max_units, s);
+  return launch_kernel<1, 3, 1>(ma, mb, mbs, p, max_units, s);
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    n = v;
+  }
+  return n;
+}
+
+}  // namespace gemms

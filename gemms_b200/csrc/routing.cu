@@ -1,0 +1,288 @@
+// routing.cu -- DeepSeek-V3 no-aux grouped router, M-tile planning and
+// deterministic expert-grouped row assignment.
+//
+// Reference: routing in flashinfer_baseline.py:95-127 (the oracle);
+// routing_topk_kernel persistent_kernel2.cu:153-299 and
+// routing_permute_kernel persistent_kernel2.cu:308-346 (the reference's GPU
+// attempt, which hard-codes group size 32, uses ex2.approx for the sigmoid
+// and assigns rows with atomics, i.e. in nondeterministic order).
+#include "common.cuh"
+#include <cfloat>
+
+namespace gemms {
+namespace {
+
+constexpr int kMaxV = 8;  // experts per lane: E <= 256
+
+struct Top2 {
+  float a, b;  // a >= b
+};
+
+__device__ __forceinline__ Top2 merge_top2(Top2 x, Top2 y) {
+  Top2 r;
+  r.a = fmaxf(x.a, y.a);
+  r.b = fmaxf(fminf(x.a, y.a), fmaxf(x.b, y.b));
+  return r;
+}
+
+// (value, index) arg-max with ties broken towards the smaller index.
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi) {
+  if (ov > v || (ov == v && oi < i)) {
+    v = ov;
+    i = oi;
+  }
+}
+
+// One warp per token.  Lane l holds experts e = j*32 + l (j < V).
+// Sigmoid: exp is evaluated in double and rounded to fp32 (correctly rounded
+// in practice), then 1/(1+e) and + bias in IEEE fp32 -- the oracle computes
+// the same values (oracle/reference_moe.py: sigmoid_exact).
+__global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= a.T) return;
+  const int E = a.E;
+  const int V = (E + 31) >> 5;
+  const int gs = E / a.n_group;  // power of two in [2, 32]
+
+  float s[kMaxV], sb[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) {
+    s[j] = 0.f;
+    sb[j] = -INFINITY;
+    const int e = j * 32 + lane;
+    if (j < V && e < E) {
+      const float x = __ldg(a.logits + (size_t)t * E + e);
+      const float ex = static_cast<float>(exp(-static_cast<double>(x)));
+      s[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+      const float bias = a.bias_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[e])
+                                     : reinterpret_cast<const float*>(a.bias)[e];
+      sb[j] = __fadd_rn(s[j], bias);
+    }
+  }
+
+  // Group score = sum of the two largest biased scores of the group
+  // (flashinfer_baseline.py:108-109).  Groups are aligned lane segments of
+  // width gs within one register j, so a segmented butterfly computes them.
+  float gscore[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) {
+    Top2 t2{sb[j], -INFINITY};
+    for (int off = 1; off < gs; off <<= 1) {
+      Top2 o{__shfl_xor_sync(0xffffffffu, t2.a, off), __shfl_xor_sync(0xffffffffu, t2.b, off)};
+      t2 = merge_top2(t2, o);
+    }
+    gscore[j] = __fadd_rn(t2.a, t2.b);
+  }
+
+  // Keep the topk_group best groups (:112-115).  Group id of (j, lane) is
+  // (j*32 + lane) / gs; one lane per group segment proposes its score.
+  bool kept[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) kept[j] = false;
+  for (int it = 0; it < a.topk_group; ++it) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int e = j * 32 + lane;
+      if (j < V && e < E && (lane % gs) == 0 && !kept[j]) argmax_merge(bv, bi, gscore[j], e / gs);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      argmax_merge(bv, bi, ov, oi);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int e = j * 32 + lane;
+      if (j < V && e < E && e / gs == bi) kept[j] = true;
+    }
+  }
+
+  // Top-k over biased scores of experts in kept groups (:118-120).
+  float cand[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) cand[j] = kept[j] ? sb[j] : -INFINITY;
+  int my_e = -1;
+  float my_s = 0.f;
+  for (int it = 0; it < a.top_k; ++it) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int e = j * 32 + lane;
+      if (cand[j] > bv || (cand[j] == bv && cand[j] > -INFINITY && e < bi)) {
+        bv = cand[j];
+        bi = e;
+        bs = s[j];
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    if (lane == it) {
+      my_e = bi;
+      my_s = bs;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j)
+      if (j * 32 + lane == bi) cand[j] = -INFINITY;
+  }
+
+  // weights = s / (sum of selected s + 1e-20) * rsf  (:123-127)
+  float sum = (lane < a.top_k) ? my_s : 0.f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  sum = __fadd_rn(sum, 1e-20f);
+  if (lane < a.top_k) {
+    const size_t o = (size_t)t * a.top_k + lane;
+    a.topk_idx[o] = my_e;
+    a.topk_w[o] = __fmul_rn(__fdiv_rn(my_s, sum), a.rsf);
+    if (a.pair_row) a.pair_row[o] = -1;
+    const int le = my_e - a.local_offset;
+    if (a.counts && le >= 0 && le < a.E_local) atomicAdd(a.counts + le, 1);
+  }
+}
+
+// Single block: per-group exclusive offsets and the 128-row M-tile list.
+__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
+  __shared__ int s_tiles[1024];
+  __shared__ int s_rows[1024];
+  const int groups = a.E_local + (a.shared_rows > 0 ? 1 : 0);
+  const int tid = threadIdx.x;
+  int rows_total = 0, tiles_total = 0;
+  // Chunked scan over groups (groups may exceed blockDim in principle).
+  for (int base = 0; base < groups; base += blockDim.x) {
+    const int g = base + tid;
+    int c = 0;
+    if (g < groups) c = (g < a.E_local) ? a.counts[g] : a.shared_rows;
+    s_rows[tid] = c;
+    s_tiles[tid] = (c + kBlock - 1) / kBlock;
+    __syncthreads();
+    for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+      int vr = 0, vt = 0;
+      if (tid >= off) {
+        vr = s_rows[tid - off];
+        vt = s_tiles[tid - off];
+      }
+      __syncthreads();
+      s_rows[tid] += vr;
+      s_tiles[tid] += vt;
+      __syncthreads();
+    }
+    const int incl_r = s_rows[tid], incl_t = s_tiles[tid];
+    const int row0 = rows_total + incl_r - c;
+    const int tile0 = tiles_total + incl_t - (c + kBlock - 1) / kBlock;
+    if (g < groups) {
+      a.offsets[g] = row0;
+      const int nt = (c + kBlock - 1) / kBlock;
+      for (int i = 0; i < nt; ++i) {
+        const int ti = tile0 + i;
+        if (ti < a.max_tiles) {
+          a.tile_group[ti] = g;
+          a.tile_row0[ti] = row0 + i * kBlock;
+          a.tile_rows[ti] = min(kBlock, c - i * kBlock);
+        } else {
+          atomicOr(a.err, kErrRowOverflow);
+        }
+      }
+    }
+    rows_total += s_rows[blockDim.x - 1];
+    tiles_total += s_tiles[blockDim.x - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    a.offsets[groups] = rows_total;
+    a.num_tiles[0] = min(tiles_total, a.max_tiles);
+  }
+}
+
+// One block per local expert: rows are assigned in increasing token order,
+// so the grouped layout is deterministic (unlike atomics-based permutes).
+__global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  const int le = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  if (le == a.E_local) {  // shared expert group: row offsets[E_local] + t
+    const int r0 = a.offsets[a.E_local];
+    for (int t = tid; t < a.T; t += blockDim.x) {
+      a.row_token[r0 + t] = t;
+      a.row_weight[r0 + t] = 1.0f;
+    }
+    return;
+  }
+  const int ge = a.local_offset + le;
+  if (tid == 0) s_base = a.offsets[le];
+  __syncthreads();
+  for (int t0 = 0; t0 < a.T; t0 += blockDim.x) {
+    const int t = t0 + tid;
+    int jsel = -1;
+    if (t < a.T) {
+      for (int j = 0; j < a.top_k; ++j)
+        if (a.topk_idx[(size_t)t * a.top_k + j] == ge) jsel = j;
+    }
+    const unsigned ballot = __ballot_sync(0xffffffffu, jsel >= 0);
+    if (lane == 0) s_warp[warp] = __popc(ballot);
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < nwarps ? s_warp[lane] : 0;
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+      }
+      if (lane < nwarps) s_warp[lane] = v;  // inclusive
+    }
+    __syncthreads();
+    const int warp_excl = (warp > 0 ? s_warp[warp - 1] : 0);
+    const int base = s_base;
+    if (jsel >= 0) {
+      const int r = base + warp_excl + __popc(ballot & ((1u << lane) - 1u));
+      const size_t o = (size_t)t * a.top_k + jsel;
+      a.row_token[r] = t;
+      a.row_weight[r] = a.topk_w[o];
+      a.pair_row[o] = r;
+    }
+    __syncthreads();
+    if (tid == 0) s_base = base + s_warp[nwarps - 1];
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+int launch_route(const RouteArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return GEMMS_OK;
+  const int warps_per_block = 8;
+  route_kernel<<<cdiv(a.T, warps_per_block), warps_per_block * 32, 0, s>>>(a);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int launch_plan(const PlanArgs& a, cudaStream_t s) {
+  plan_kernel<<<1, 1024, 0, s>>>(a);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int launch_assign(const AssignArgs& a, cudaStream_t s) {
+  const int blocks = a.E_local + (a.shared_rows > 0 ? 1 : 0);
+  if (blocks == 0 || a.T <= 0) return GEMMS_OK;
+  assign_kernel<<<blocks, 1024, 0, s>>>(a);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+}  // namespace gemms

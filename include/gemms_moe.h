@@ -1,0 +1,134 @@
+/*
+ * gemms_moe.h -- C ABI of the B200-native DeepSeek-V3 FP8 MoE layer.
+ *
+ * Plain pointers and sizes only; the caller owns every buffer.  All entry
+ * points are stream-ordered (nothing synchronises the host unless the name
+ * says so) and return 0 on success or a negative GEMMS_ERR_* code.  No entry
+ * point calls exit().
+ *
+ * Reference interfaces replaced (plops655/GEMMS):
+ *   gemms_moe_fwd        <- launch_persistent_moe_v2(...)      persistent_kernel2.cu:896-910
+ *                           and the operator run(...)           flashinfer_baseline.py:5-16
+ *   gemms_route          <- routing_topk_kernel                 persistent_kernel2.cu:153-299
+ *   gemms_expert_ffn     <- persistent_gemm_kernel phases 1+2   persistent_kernel2.cu:388-890
+ *   gemms_moe_workspace_size <- ScratchOffsets2 / compute_scratch_offsets2
+ *                                                               persistent_kernel2.cu:32-67
+ *   gemms_strerror       <- CUDA_CHECK's message+exit           common.h:8-15
+ */
+#ifndef GEMMS_MOE_H_
+#define GEMMS_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* gemms_stream_t;
+
+enum {
+  GEMMS_OK = 0,
+  GEMMS_ERR_SHAPE = -1,      /* unsupported or inconsistent geometry            */
+  GEMMS_ERR_ALIGN = -2,      /* a pointer is not 16-byte aligned                */
+  GEMMS_ERR_WORKSPACE = -3,  /* workspace missing or smaller than required      */
+  GEMMS_ERR_CUDA = -4,       /* a CUDA runtime call failed                      */
+  GEMMS_ERR_TIMEOUT = -5,    /* a device-side wait gave up (error word set)     */
+  GEMMS_ERR_DRIVER = -6,     /* cuTensorMapEncodeTiled unavailable or failed    */
+  GEMMS_ERR_DEVICE = -7,     /* current device is not sm_100                    */
+  GEMMS_ERR_ARG = -8,        /* a required pointer is NULL                      */
+  GEMMS_ERR_CAPACITY = -9    /* a size exceeds a fixed capacity of this entry   */
+};
+
+/* Activation input formats. */
+enum {
+  GEMMS_INPUT_BF16 = 0,      /* x bf16 [T,H]; quantised per 1x128 inside        */
+  GEMMS_INPUT_FP8 = 1        /* e4m3 [T,H] + fp32 scale [H/128, T] (run())      */
+};
+
+typedef struct {
+  int32_t T;                    /* tokens                                          */
+  int32_t H;                    /* hidden size, multiple of 128                    */
+  int32_t I;                    /* expert intermediate size, multiple of 128       */
+  int32_t E;                    /* routed experts (width of the logits)            */
+  int32_t E_local;              /* experts whose weights are passed                */
+  int32_t local_expert_offset;  /* global id of local expert 0                     */
+  int32_t n_group;              /* routing groups; E/n_group in {2,4,8,16,32}      */
+  int32_t topk_group;           /* groups kept per token                           */
+  int32_t top_k;                /* experts per token, <= 16                        */
+  int32_t has_shared;           /* 1: a shared expert (weight 1.0) is applied      */
+  int32_t input_mode;           /* GEMMS_INPUT_*                                   */
+  int32_t bias_bf16;            /* 1: routing_bias is bf16, 0: fp32                */
+  int32_t inter_planes;         /* e4m3 planes of the SwiGLU intermediate: 2 or 3  */
+  float routed_scaling_factor;
+} GemmsMoeShape;
+
+typedef struct {
+  GemmsMoeShape shape;
+  const float* routing_logits;      /* fp32 [T, E]                                 */
+  const void* routing_bias;         /* fp32 or bf16 [E]                            */
+  const void* hidden_bf16;          /* bf16 [T, H]       (GEMMS_INPUT_BF16)        */
+  const void* hidden_fp8;           /* e4m3 [T, H]       (GEMMS_INPUT_FP8)         */
+  const float* hidden_scale;        /* fp32 [H/128, T]   (GEMMS_INPUT_FP8)         */
+  const void* w13;                  /* e4m3 [E_local, 2I, H]                       */
+  const float* w13_scale;           /* fp32 [E_local, 2I/128, H/128]               */
+  const void* w2;                   /* e4m3 [E_local, H, I]                        */
+  const float* w2_scale;            /* fp32 [E_local, H/128, I/128]                */
+  const void* shared_w13;           /* e4m3 [2I, H]          (has_shared)          */
+  const float* shared_w13_scale;    /* fp32 [2I/128, H/128]  (has_shared)          */
+  const void* shared_w2;            /* e4m3 [H, I]           (has_shared)          */
+  const float* shared_w2_scale;     /* fp32 [H/128, I/128]   (has_shared)          */
+  void* out;                        /* bf16 [T, H], written (not accumulated)      */
+  int32_t* topk_idx_out;            /* optional int32 [T, top_k] (NULL: skip)      */
+  float* topk_w_out;                /* optional fp32 [T, top_k]                    */
+  int32_t* expert_counts_out;       /* optional int32 [E_local]                    */
+} GemmsMoeArgs;
+
+/* Bytes of device workspace gemms_moe_fwd needs for this shape. */
+size_t gemms_moe_workspace_size(const GemmsMoeShape* shape);
+
+/* Full layer forward: route -> permute(+quant) -> GEMM1+SwiGLU -> GEMM2 ->
+ * weighted combine (+ shared expert) -> bf16.  Workspace must be 256-byte
+ * aligned and at least gemms_moe_workspace_size() bytes; the contents need no
+ * initialisation.  Concurrent calls need distinct workspaces. */
+int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, gemms_stream_t stream);
+
+/* Router only (for tests and expert-parallel dispatch): fp32 logits [T,E] +
+ * bias -> topk_idx int32 [T,top_k] (descending biased score), topk_w fp32
+ * [T,top_k] (normalised, times the scaling factor), and counts int32 [E]
+ * (histogram over all E experts; must be zeroed by the caller). */
+int gemms_route(const float* logits, const void* bias, int32_t bias_bf16, int32_t T, int32_t E,
+                int32_t n_group, int32_t topk_group, int32_t top_k, float routed_scaling_factor,
+                int32_t* topk_idx, float* topk_w, int32_t* counts, gemms_stream_t stream);
+
+/* Expert FFN over rows that are already grouped by expert (expert-parallel
+ * receive side): rows [0, R) hold e4m3 activations [R, H] with scales
+ * [H/128, R] (row-major per 128-column block, leading dimension R);
+ * expert_counts[E_local] (device) gives how many consecutive rows belong to
+ * each local expert, in order.  Row r's result times row_weight[r] is added
+ * into out_f32[row_dest[r], :] (fp32 [n_dest, H], accumulated, not zeroed).
+ * Workspace: gemms_expert_ffn_workspace_size(). */
+size_t gemms_expert_ffn_workspace_size(int32_t R_max, int32_t H, int32_t I, int32_t E_local,
+                                       int32_t inter_planes);
+int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_max,
+                     const int32_t* expert_counts, const int32_t* row_dest, const float* row_weight,
+                     int32_t H, int32_t I, int32_t E_local, int32_t inter_planes,
+                     const void* w13, const float* w13_scale, const void* w2, const float* w2_scale,
+                     float* out_f32, void* workspace, size_t ws_bytes, gemms_stream_t stream);
+
+/* Reads and clears the device error word kept in a gemms_moe_fwd workspace.
+ * Synchronises the stream.  *flags receives the raw bit set (0 = clean). */
+int gemms_moe_check(void* workspace, gemms_stream_t stream, int32_t* flags);
+
+/* Static description of an error code. */
+const char* gemms_strerror(int code);
+
+/* Library version string. */
+const char* gemms_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMMS_MOE_H_ */

@@ -1,0 +1,68 @@
+"""CPU: the C-ABI library loads and exports every symbol include/gemms_moe.h declares."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import gemms_b200
+from gemms_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+
+
+def declared_symbols():
+    syms = set()
+    for fn in os.listdir(HEADER):
+        if fn.endswith(".h"):
+            txt = open(os.path.join(HEADER, fn)).read()
+            txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+            syms |= set(re.findall(r"\b(gemms_[a-z0-9_]+)\s*\(", txt))
+    return syms
+
+
+def test_library_loads_and_exports_all_symbols():
+    L = gemms_b200.load_library()
+    syms = declared_symbols()
+    assert "gemms_moe_fwd" in syms and len(syms) >= 8
+    for s in syms:
+        assert hasattr(L, s), f"{s} declared in include/ but not exported"
+    assert set(_lib.EXPORTS) <= syms
+
+
+def test_version_and_strerror():
+    L = gemms_b200.load_library()
+    assert b"sm_100a" in L.gemms_version()
+    for code in range(0, -10, -1):
+        assert L.gemms_strerror(code)
+    assert L.gemms_strerror(-99) == b"unknown error"
+
+
+def test_workspace_size_and_shape_rejection():
+    L = gemms_b200.load_library()
+    s = _lib.GemmsMoeShape(T=4096, H=7168, I=2048, E=256, E_local=256, n_group=8, topk_group=4, top_k=8,
+                           has_shared=1, input_mode=0, inter_planes=2, routed_scaling_factor=2.5)
+    n = L.gemms_moe_workspace_size(ctypes.byref(s))
+    assert 400e6 < n < 700e6
+    bad = _lib.GemmsMoeShape(**{f: getattr(s, f) for f, _ in _lib.GemmsMoeShape._fields_})
+    bad.n_group = 7  # 256 % 7 != 0
+    assert L.gemms_moe_workspace_size(ctypes.byref(bad)) == 0
+    bad.n_group = 8
+    bad.top_k = 17
+    assert L.gemms_moe_workspace_size(ctypes.byref(bad)) == 0
+    assert L.gemms_expert_ffn_workspace_size(1024, 7168, 2048, 32, 2) > 0
+    assert L.gemms_expert_ffn_workspace_size(1024, 7000, 2048, 32, 2) == 0
+
+
+def test_fwd_rejects_null_args_without_gpu():
+    L = gemms_b200.load_library()
+    assert L.gemms_moe_fwd(None, None, 0, None) == -8  # GEMMS_ERR_ARG
+
+
+def test_operators_refuse_cpu_tensors():
+    import torch
+    x = torch.zeros(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(gemms_b200.ShapeError):
+        gemms_b200.moe(x, torch.zeros(8, 256), torch.zeros(8), torch.zeros(8, 256, 256).to(torch.float8_e4m3fn),
+                       torch.ones(8, 2, 2), torch.zeros(8, 256, 128).to(torch.float8_e4m3fn), torch.ones(8, 2, 1),
+                       n_group=4, topk_group=2, top_k=2)

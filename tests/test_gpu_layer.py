@@ -1,0 +1,154 @@
+"""GPU: full MoE layer parity against the oracle and the reference's golden outputs."""
+import pytest
+import torch
+
+import gemms_b200
+from gemms_b200 import workloads as W
+from oracle import reference_moe as R
+from tests import helpers as Hh
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def golden():
+    g = Hh.load_golden()
+    d = Hh.golden_weights(g)
+    return g, d
+
+
+@pytest.mark.parametrize("off", [0, 96, 224])
+def test_run_matches_reference_golden(golden, off):
+    """gemms_b200.run on the inputs the reference's own run() produced outputs for."""
+    g, d = golden
+    dev = {k: v.cuda() for k, v in d.items() if isinstance(v, torch.Tensor)}
+    out, idx, w, counts = gemms_b200.run(g["routing_logits"].cuda(), g["routing_bias"].cuda(),
+                                         g["hidden_states"].cuda(), g["hidden_states_scale"].cuda(), dev["w13"],
+                                         dev["w13_scale"], dev["w2"], dev["w2_scale"], off, 2.5,
+                                         return_routing=True)
+    gemms_b200.check_device_errors(tag="run")
+    ref = Hh.golden_out(g, off)
+    Hh.assert_parity(out, ref, f"run(off={off})")
+    ridx, _, _, _ = R.route(g["routing_logits"], g["routing_bias"], 8, 4, 8, 2.5)
+    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
+    loc = ridx[(ridx >= off) & (ridx < off + 32)] - off
+    assert torch.equal(counts.cpu().long(), torch.bincount(loc, minlength=32))
+
+
+def _moe_case(sh, seed, planes=2, device_inputs=True):
+    d = W.make_inputs(sh, seed=seed)
+    dd = Hh.to_dev(d)
+    kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
+              inter_planes=planes)
+    shared = {k: dd[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale") if k in dd}
+    out, idx, w, counts, logits = gemms_b200.moe(dd["x"], dd["router_w"], dd["router_bias"], dd["w13"],
+                                                 dd["w13_scale"], dd["w2"], dd["w2_scale"], return_routing=True,
+                                                 **shared, **kw)
+    gemms_b200.check_device_errors(tag="moe")
+    # routing parity at the reference boundary: identical fp32 logits in
+    lg = logits.cpu()
+    ref_logits = R.router_logits(d["x"], d["router_w"])
+    torch.testing.assert_close(lg, ref_logits, rtol=1e-4, atol=2e-5)
+    ref = R.moe_layer(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+                      d.get("shared_w13"), d.get("shared_w13_scale"), d.get("shared_w2"), d.get("shared_w2_scale"),
+                      n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, rsf=sh.rsf, logits=lg)
+    ridx, _, _, _ = R.route(lg, d["router_bias"], sh.n_group, sh.topk_group, sh.top_k, sh.rsf)
+    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
+    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=sh.E))
+    return out, ref
+
+
+def test_moe_c0():
+    out, ref = _moe_case(W.CONFIGS["c0"], seed=0)
+    m = Hh.assert_parity(out, ref, "c0")
+    print("c0 parity", m)
+
+
+def test_moe_c0_three_planes():
+    out, ref = _moe_case(W.CONFIGS["c0"], seed=1, planes=3)
+    m = Hh.assert_parity(out, ref, "c0 planes=3")
+    assert m["mae_rms"] < 2e-4
+
+
+@pytest.mark.parametrize("T", [1, 3, 130, 300])
+def test_moe_c0_ragged_T_with_shared(T):
+    sh = W.CONFIGS["c0"].replace(T=T, shared=True)
+    out, ref = _moe_case(sh, seed=T)
+    Hh.assert_parity(out, ref, f"c0 T={T} shared")
+
+
+def test_run_expert_slice_without_hits():
+    """Local expert slice that no token routes to: output is exactly zero."""
+    g = torch.Generator().manual_seed(9)
+    T, H, I, E = 16, 256, 128, 32
+    logits = torch.full((T, E), -8.0)
+    logits[:, :8] = torch.randn(T, 8, generator=g) + 4  # everyone picks experts 0..7
+    bias = torch.zeros(E)
+    hs = torch.randn(T, H, generator=g).to(torch.float8_e4m3fn)
+    hss = torch.ones(H // 128, T)
+    w13 = torch.randn(8, 2 * I, H, generator=g).to(torch.float8_e4m3fn)
+    w2 = torch.randn(8, H, I, generator=g).to(torch.float8_e4m3fn)
+    s13 = torch.full((8, 2 * I // 128, H // 128), 1e-3)
+    s2 = torch.full((8, H // 128, I // 128), 1e-3)
+    out = gemms_b200.run(logits.cuda(), bias.cuda(), hs.cuda(), hss.cuda(), w13.cuda(), s13.cuda(), w2.cuda(),
+                         s2.cuda(), 24, 2.5, n_group=4, topk_group=2, top_k=4)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out) == 0
+    ref = R.run_local(logits, bias, hs, hss, w13, s13, w2, s2, 0, 2.5, n_group=4, topk_group=2, top_k=4)
+    out0 = gemms_b200.run(logits.cuda(), bias.cuda(), hs.cuda(), hss.cuda(), w13.cuda(), s13.cuda(), w2.cuda(),
+                          s2.cuda(), 0, 2.5, n_group=4, topk_group=2, top_k=4)
+    Hh.assert_parity(out0, ref, "slice 0")
+
+
+def test_shape_errors_raise():
+    x = torch.zeros(4, 7168, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(AssertionError):  # reference-style assertion semantics
+        gemms_b200.run(torch.zeros(4, 256, device="cuda"), torch.zeros(256, device="cuda"),
+                       x.to(torch.float8_e4m3fn), torch.ones(55, 4, device="cuda"),
+                       torch.zeros(32, 4096, 7168, device="cuda", dtype=torch.float8_e4m3fn),
+                       torch.ones(32, 32, 56, device="cuda"),
+                       torch.zeros(32, 7168, 2048, device="cuda", dtype=torch.float8_e4m3fn),
+                       torch.ones(32, 56, 16, device="cuda"), 0, 2.5)
+
+
+def _cpu_weights_for(d_dev, experts):
+    """CPU copies of only the experts the sampled tokens use (others left unset)."""
+    E = d_dev["w13"].shape[0]
+    out = {}
+    for k in ("w13", "w13_scale", "w2", "w2_scale"):
+        t = torch.empty(d_dev[k].shape, dtype=d_dev[k].dtype)
+        for e in experts:
+            t[e] = d_dev[k][e].cpu()
+        out[k] = t
+    return out
+
+
+@pytest.mark.slow
+def test_moe_c1_full_size_sampled_tokens():
+    """Config c1 (T=4096, full V3 + shared expert): routing of all tokens exact,
+    output rows of a token sample within the parity bar."""
+    sh = W.CONFIGS["c1"]
+    d = W.make_inputs(sh, seed=0, device="cuda")
+    out, idx, w, counts, logits = gemms_b200.moe(
+        d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+        shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
+        shared_w2_scale=d["shared_w2_scale"], return_routing=True)
+    gemms_b200.check_device_errors(tag="moe")
+    lg = logits.cpu()
+    bias = d["router_bias"].cpu()
+    ridx, _, _, _ = R.route(lg, bias, 8, 4, 8, 2.5)
+    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
+    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=256))
+    assert int(counts.sum()) == 4096 * 8
+    rows = [0, 1, 777, 2048, 4095]
+    experts = sorted(set(ridx[rows].reshape(-1).tolist()))
+    cw = _cpu_weights_for(d, experts)
+    x = d["x"].cpu()
+    ref = R.moe_layer(x, d["router_w"].cpu(), bias, cw["w13"], cw["w13_scale"], cw["w2"], cw["w2_scale"],
+                      d["shared_w13"].cpu(), d["shared_w13_scale"].cpu(), d["shared_w2"].cpu(),
+                      d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg,
+                      tokens=rows)
+    m = Hh.assert_parity(out, ref, "c1 sampled", rows=rows)
+    print("c1 sampled parity", m)
+    o = out.float()
+    assert torch.isfinite(o).all()

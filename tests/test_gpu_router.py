@@ -1,0 +1,66 @@
+"""GPU: the CUDA router against the oracle's routing (flashinfer_baseline.py:95-127).
+
+Top-k expert sets and per-expert counts must match bit for bit given identical
+fp32 logits; normalised weights to fp32 rounding.
+"""
+import pytest
+import torch
+
+import gemms_b200
+from gemms_b200 import workloads as W
+from oracle import reference_moe as R
+from tests import helpers as Hh
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(logits, bias, ng, tg, k, rsf=2.5):
+    idx, w, counts = gemms_b200.route(logits.cuda(), bias.cuda(), n_group=ng, topk_group=tg, top_k=k,
+                                      routed_scaling_factor=rsf)
+    torch.cuda.synchronize()
+    ref_idx, ref_w, _, sb = R.route(logits.cpu(), bias.cpu().float(), ng, tg, k, rsf, exact_exp=True)
+    ref_idx_t, _, _, _ = R.route(logits.cpu(), bias.cpu().float(), ng, tg, k, rsf, exact_exp=False)
+    got = Hh.sorted_sets(idx)
+    eg, gg = R.routing_margins(sb, ref_idx, ng, tg)
+    diag = f"min expert gap {float(eg.min()):.3e}, min group gap {float(gg.min()):.3e}"
+    assert torch.equal(got, Hh.sorted_sets(ref_idx)), "top-k sets differ from oracle (exact exp); " + diag
+    assert torch.equal(got, Hh.sorted_sets(ref_idx_t)), "top-k sets differ from oracle (torch exp); " + diag
+    E = logits.shape[1]
+    ref_counts = torch.bincount(ref_idx.reshape(-1), minlength=E)
+    assert torch.equal(counts.cpu().long(), ref_counts)
+    # weights: gather dense oracle weights at the selected experts
+    wg = torch.gather(ref_w, 1, idx.cpu().long())
+    torch.testing.assert_close(w.cpu(), wg, rtol=2e-6, atol=1e-7)
+    assert torch.all(w.cpu() > 0)
+
+
+@pytest.mark.parametrize("cfg,T", [("c0", 64), ("c1", 4096), ("c1", 1), ("c1", 33)])
+def test_router_matches_oracle(cfg, T):
+    sh = W.CONFIGS[cfg].replace(T=T)
+    d = W.make_inputs(sh, seed=11, with_weights=False)
+    logits = R.router_logits(d["x"], d["router_w"])
+    _check(logits, d["router_bias"], sh.n_group, sh.topk_group, sh.top_k)
+
+
+@pytest.mark.parametrize("E,ng,tg,k", [(64, 32, 4, 4), (128, 8, 3, 6), (256, 16, 8, 16), (32, 2, 1, 3), (16, 4, 2, 2)])
+def test_router_geometries(E, ng, tg, k):
+    g = torch.Generator().manual_seed(E * 7 + k)
+    logits = torch.randn(300, E, generator=g) * 2
+    bias = (torch.rand(E, generator=g) - 0.5) * 0.2
+    _check(logits, bias, ng, tg, k)
+
+
+def test_router_bf16_bias():
+    g = torch.Generator().manual_seed(2)
+    logits = torch.randn(512, 256, generator=g) * 1.7
+    bias = ((torch.rand(256, generator=g) - 0.5) * 0.2).bfloat16()
+    _check(logits, bias, 8, 4, 8)
+
+
+def test_router_large_logits_saturate():
+    # |logit| large: sigmoid saturates to 0/1; ties among saturated scores are
+    # broken by bias, all finite.
+    g = torch.Generator().manual_seed(4)
+    logits = torch.randn(64, 256, generator=g) * 60
+    bias = (torch.rand(256, generator=g) - 0.5) * 0.2
+    _check(logits, bias, 8, 4, 8)
