@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 DeepSeek-V3 FP8 MoE layer (the hot path of plops655/GEMMS).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gemms|reference]
+
+One *step* is one full MoE layer forward (router GEMM -> routing -> permute +
+1x128 quant -> grouped FP8 GEMM1 + SwiGLU -> grouped FP8 GEMM2 -> weighted
+combine + shared expert -> bf16) over one batch of synthetic tokens.
+
+* N=1: BASELINE config c1 -- T=4096, H=7168, I=2048, E=256, 8 groups /
+  top-4 groups / top-8, scaling 2.5, + 1 shared expert.  Inputs are resident in
+  HBM; every step streams 11.3 GB of expert weights, far larger than the 126 MB
+  L2, so no flush is needed between steps.
+* N>1 (torchrun): BASELINE config c3 -- expert-parallel over N ranks, T=32768
+  tokens in total (32768/N per rank), E/N experts per rank, NCCL all-to-all.
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
+implementation of the path (the oracle restatement in ``oracle/``, bit-identical
+to ``flashinfer_baseline.run``) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE layer tokens/s and FP8 TFLOP/s (frac of peak) at T=4096, 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["gemms", "reference"], default="gemms")
+    p.add_argument("--config", default=None, help="c1 (N=1 default), c2:<T> decode, c3 (N>1 default), c4")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
+    return p.parse_args()
+
+
+def parse_config(spec: str):
+    """'c1', 'c2:128' (decode T) or 'c1:T=1024,E=64' (overrides for profiling)."""
+    from gemms_b200 import workloads as W
+
+    name, _, rest = spec.partition(":")
+    base = W.CONFIGS[name]
+    if rest:
+        if "=" not in rest:
+            return base.replace(T=int(rest))
+        kv = {}
+        for item in rest.split(","):
+            k, v = item.split("=")
+            kv[k] = type(getattr(base, k))(v) if not isinstance(getattr(base, k), bool) else v.lower() in ("1", "true")
+        base = base.replace(**kv)
+    return base
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                pw.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        # samples under load: power within 70% of the region's max
+        pmax = max(pw)
+        loaded = [s for s, p in zip(sm, pw) if p >= 0.7 * pmax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": pmax}
+
+
+# ------------------------------------------------------------ workload sizes
+def algorithmic_bytes(sh, counts, planes: int, world: int = 1):
+    """HBM bytes the two grouped GEMMs must move per launch (not counting
+    re-reads): weights + scales of every expert that received rows (+ shared),
+    the grouped activation rows, and the SwiGLU intermediate (written by GEMM1,
+    read by GEMM2), plus GEMM2's fp32 output accumulation."""
+    H, I = sh.H, sh.I
+    hit = int((counts > 0).sum())
+    rows = int(counts.sum()) + (sh.T if sh.shared else 0)
+    n_exp = hit + (1 if sh.shared else 0)
+    w13 = 2 * I * H + 4 * (2 * I // 128) * (H // 128)
+    w2 = H * I + 4 * (H // 128) * (I // 128)
+    a_rows = rows * (H + 4 * H // 128)
+    inter = rows * (planes * I + 4 * I // 128)
+    out_acc = sh.T * H * 4 * 2  # fp32 accumulation target, read+write once
+    g1 = n_exp * w13 + a_rows + inter
+    g2 = n_exp * w2 + inter + out_acc
+    return {"gemm1": g1, "gemm2": g2, "experts_hit": hit, "rows": rows}
+
+
+def _traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu capture summary, if any."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(kernel)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_baseline(sh, d_dev, logits_dev, n_experts_sample: int, threads: int | None = None):
+    """Time the oracle port (== reference run(), bit for bit) on host cores for
+    a bounded sample: ``n_experts_sample`` of the E routed experts over all T
+    tokens, plus the shared expert; scaled to the full layer."""
+    import torch
+
+    from oracle import reference_moe as R
+
+    if threads:
+        torch.set_num_threads(threads)
+    nt = torch.get_num_threads()
+    x = d_dev["x"].cpu()
+    logits = logits_dev.cpu()
+    bias = d_dev["router_bias"].cpu()
+    hs, hss = R.quantize_1x128(x)
+    n = n_experts_sample
+    w13 = d_dev["w13"][:n].cpu()
+    w13s = d_dev["w13_scale"][:n].cpu()
+    w2 = d_dev["w2"][:n].cpu()
+    w2s = d_dev["w2_scale"][:n].cpu()
+    t0 = time.perf_counter()
+    R.run_local(logits, bias, hs, hss, w13, w13s, w2, w2s, 0, sh.rsf, n_group=sh.n_group,
+                topk_group=sh.topk_group, top_k=sh.top_k, return_fp32=True)
+    t_chunk = time.perf_counter() - t0
+    t_shared = 0.0
+    if sh.shared:
+        A = R.dequant_hidden(hs, hss)
+        sw = [d_dev[k].cpu() for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale")]
+        t0 = time.perf_counter()
+        R.shared_expert(A, *sw)
+        t_shared = time.perf_counter() - t0
+    t_layer = t_chunk * (sh.E / n) + t_shared
+    return {"value": sh.T / t_layer, "unit": "tokens/s", "cores": nt, "kind": "port",
+            "sample": f"oracle run_local (== reference run()) over all T={sh.T} tokens for {n} of {sh.E} experts "
+                      f"({t_chunk:.2f} s) + shared expert ({t_shared:.2f} s), scaled x{sh.E / n:.0f} to the full "
+                      f"layer ({t_layer:.1f} s)",
+            "os_cpu_count": os.cpu_count()}
+
+
+def reference_arm(a, sh):
+    """--impl reference: the reference's CPU path (oracle port) on host cores.
+    One step = one call of the reference's run() over all T tokens with
+    E_local=8 local experts (1/32 of the routed experts; the reference's own
+    calls use E_local=32, so each step charges the per-call activation dequant
+    and routing 4x more often than the reference would -- a conservative,
+    slightly slow figure for the CPU).  Throughput scales by (E+1)/8 units."""
+    import torch
+
+    from gemms_b200 import workloads as W
+    from oracle import reference_moe as R
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    per_step = 8
+    d = W.make_inputs(sh, seed=0, experts=per_step)
+    logits = R.router_logits(d["x"], d["router_w"])
+    hs, hss = R.quantize_1x128(d["x"])
+    # Make expert 0 receive its typical share: route with the real logits.
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        R.run_local(logits, d["router_bias"], hs, hss, d["w13"], d["w13_scale"], d["w2"], d["w2_scale"], 0,
+                    sh.rsf, n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, return_fp32=True)
+        dt = time.perf_counter() - t0
+        if i >= a.warmup:
+            times.append(dt)
+    units = (sh.E + (1 if sh.shared else 0)) / per_step
+    ms = statistics.mean(times) * 1e3
+    value = (sh.T / units) / (ms / 1e3)
+    cores = torch.get_num_threads()
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (fp8 dequantised)", "data": "synthetic (seeded, BASELINE c1 shapes)",
+            "config": {"workload": "c1: DeepSeek-V3 MoE layer T=4096 H=7168 I=2048 E=256 top-8 + shared expert",
+                       "step": "one reference run() call: all 4096 tokens, E_local=8 of 256 routed experts"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "per step: oracle port of flashinfer_baseline.run (bit-identical) over "
+                                       "T=4096 tokens for 8 of 257 expert units of the c1 layer, scaled by 257/8"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+def count_kernels_per_step(step_fn) -> int:
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        if ev.device_type.name == "CUDA" and "gemms::" in ev.name:
+            n += 1
+    return n
+
+
+def gpu_arm(a):
+    import torch
+    import torch.distributed as dist
+
+    import gemms_b200
+    from gemms_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        group = dist.group.WORLD
+    cfg = a.config or ("c1" if world == 1 else "c3")
+    base = parse_config(cfg)
+    T_rank = base.T // world if world > 1 else base.T
+    sh = base.replace(T=T_rank)
+    planes = 2
+
+    # inputs: this rank's tokens; this rank's E/world experts (EP) or all E
+    n_local = sh.E // world
+    d = W.make_inputs(sh, seed=rank, device=dev, experts=n_local)
+    # every rank must hold the same router weights/bias and shared expert
+    g = torch.Generator(device=dev).manual_seed(12345)
+    d["router_w"] = torch.randn((sh.E, sh.H), generator=g, device=dev) * 0.02
+    d["router_bias"] = torch.rand((sh.E,), generator=g, device=dev) * 0.2 - 0.1
+    if sh.shared:
+        d["shared_w13"] = torch.randn((2 * sh.I, sh.H), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
+        d["shared_w13_scale"] = torch.rand((2 * sh.I // 128, sh.H // 128), generator=g, device=dev) * 2e-3 + 1e-3
+        d["shared_w2"] = torch.randn((sh.H, sh.I), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
+        d["shared_w2_scale"] = torch.rand((sh.H // 128, sh.I // 128), generator=g, device=dev) * 2e-3 + 1e-3
+    shared_kw = {k: d[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale") if k in d}
+    kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
+              inter_planes=planes, ep_group=group, **shared_kw)
+
+    def step(x, events=None):
+        if group is None:
+            return gemms_b200.moe(x, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                                  d["w2_scale"], profile_events=events, **kw)
+        return gemms_b200.moe(x, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                              d["w2_scale"], **kw)
+
+    def barrier():
+        if group is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # routing statistics for the algorithmic byte count
+    if group is None:
+        out, idx, wts, counts, logits = gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"],
+                                                       d["w13_scale"], d["w2"], d["w2_scale"], return_routing=True,
+                                                       **{k: v for k, v in kw.items() if k != "ep_group"})
+        gemms_b200.check_device_errors(tag="moe")
+        counts_cpu = counts.cpu()
+    for _ in range(a.warmup):
+        step(d["x"])
+    barrier()
+    launches_per_step = None
+    if not a.no_launch_count:
+        launches_per_step = count_kernels_per_step(lambda: step(d["x"]))
+    barrier()
+
+    # ---- device-resident timed region
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    nev = a.steps if group is None else 0
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nev)]
+    for e3 in evs:
+        for e in e3:
+            e.record()  # materialise the CUDA events before they are handed to the C ABI
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(a.steps):
+        step(d["x"], evs[i] if nev else None)
+    t1.record()
+    barrier()
+    ms_total = t0.elapsed_time(t1)
+    if group is not None:
+        tt = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    ms = ms_total / a.steps
+
+    g1_ms = statistics.mean(evs[i][0].elapsed_time(evs[i][1]) for i in range(nev)) if nev else None
+    g2_ms = statistics.mean(evs[i][1].elapsed_time(evs[i][2]) for i in range(nev)) if nev else None
+    if group is None:
+        gemms_b200.check_device_errors(tag="moe")
+
+    # ---- end-to-end through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        x_host = d["x"].cpu().pin_memory()
+        out_host = torch.empty((sh.T, sh.H), dtype=torch.bfloat16).pin_memory()
+        x_dev = torch.empty_like(d["x"])
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            y = step(x_dev)
+            out_host.copy_(y, non_blocking=True)
+        e1.record()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        if group is not None:
+            tt = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_ms = float(tt.item())
+        e2e_ms /= a.steps
+        e2e = {"value": base.T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+               "path": "pinned host x -> gemms_b200.moe (public API) -> pinned host out, every step"}
+    clocks = sampler.stop() if sampler else None
+
+    tokens_total = base.T
+    value = tokens_total / (ms / 1e3)
+    flops = 6.0 * sh.H * sh.I * (base.T * sh.top_k + (base.T if sh.shared else 0))
+    if rank != 0:
+        if group is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    hbm, bf16, src = _peaks()
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)",
+            "data": "synthetic (seeded; BASELINE distributions; random-init weights)",
+            "config": {"workload": (f"{cfg}: DeepSeek-V3 MoE layer T={base.T} H={sh.H} I={sh.I} E={sh.E} "
+                                    f"groups {sh.n_group}/{sh.topk_group} top-{sh.top_k}"
+                                    + (" + shared expert" if sh.shared else "")),
+                       "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
+                       "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"},
+            "tflops": flops / (ms / 1e3) / 1e12,
+            "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
+            "e2e": e2e, "clocks": clocks}
+    if group is None:
+        ab = algorithmic_bytes(sh, counts_cpu, planes)
+        g1_gbs = ab["gemm1"] / (g1_ms / 1e3) / 1e9
+        g2_gbs = ab["gemm2"] / (g2_ms / 1e3) / 1e9
+        tr = _traffic("gemm1")
+        line["roofline"] = {"bound": "hbm", "kernel": "grouped_gemm_kernel<0,1,2> (GEMM1 + SwiGLU + requant)",
+                            "achieved": g1_gbs, "peak": hbm, "unit": "GB/s", "frac": g1_gbs / hbm,
+                            "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else
+                            "fallback 6650 GB/s", "traffic": tr,
+                            "algorithmic_bytes": ab["gemm1"], "launch_ms": g1_ms}
+        line["kernels"] = {"gemm1": {"ms": g1_ms, "GB/s": g1_gbs, "bytes": ab["gemm1"]},
+                           "gemm2": {"ms": g2_ms, "GB/s": g2_gbs, "bytes": ab["gemm2"], "traffic": _traffic("gemm2")},
+                           "layer": {"ms": ms, "hbm_frac_of_layer_floor":
+                                     (ab["gemm1"] + ab["gemm2"]) / 1e9 / hbm / (ms / 1e3)},
+                           "experts_hit": ab["experts_hit"], "rows": ab["rows"]}
+        if not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(sh, d, logits, n_experts_sample=32)
+    print(json.dumps(line), flush=True)
+    if group is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        from gemms_b200 import workloads as W
+
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        sh = W.CONFIGS["c1"]
+        if world > 1 and int(os.environ.get("RANK", "0")) != 0:
+            return
+        reference_arm(a, sh)
+        return
+    gpu_arm(a)
+
+
+if __name__ == "__main__":
+    main()

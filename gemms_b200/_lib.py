@@ -50,6 +50,7 @@ class GemmsMoeArgs(ctypes.Structure):
         ("shared_w13", c_void_p), ("shared_w13_scale", c_void_p), ("shared_w2", c_void_p),
         ("shared_w2_scale", c_void_p),
         ("out", c_void_p), ("topk_idx_out", c_void_p), ("topk_w_out", c_void_p), ("expert_counts_out", c_void_p),
+        ("profile_events", c_void_p),
     ]
 
 

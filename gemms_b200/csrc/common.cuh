@@ -6,7 +6,7 @@
 #include <cstdint>
 #include <cstddef>
 
-#include "../../include/gemms_moe.h"
+#include "gemms_moe.h"
 
 namespace gemms {
 

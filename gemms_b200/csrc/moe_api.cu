@@ -236,7 +236,10 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   g1.inter_scale_ld = L.scale_ld;
   g1.err = err;
   if (!g1.w13) g1.w13 = g1.sw13;
+  cudaEvent_t const* evs = reinterpret_cast<cudaEvent_t const*>(args->profile_events);
+  if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[0], st));
   if ((rc = launch_gemm1(g1, st))) return rc;
+  if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[1], st));
 
   Gemm2Args g2{};
   g2.g = gg;
@@ -258,6 +261,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   g2.err = err;
   if (!g2.w2) g2.w2 = g2.sw2;
   if ((rc = launch_gemm2(g2, st))) return rc;
+  if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[2], st));
 
   if ((rc = launch_to_bf16(g2.out, static_cast<__nv_bfloat16*>(args->out), (size_t)s.T * s.H, st))) return rc;
 

@@ -178,14 +178,15 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         shared_w2: torch.Tensor | None = None, shared_w2_scale: torch.Tensor | None = None,
         n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
         inter_planes: int = 2, logits: torch.Tensor | None = None, ep_group=None,
-        return_routing: bool = False):
+        return_routing: bool = False, profile_events=None):
     """DeepSeek-V3 MoE layer forward: bf16 x [T, H] -> bf16 [T, H].
 
     ``w13`` [E, 2I, H] / ``w2`` [E, H, I] are e4m3 with fp32 128x128 block
     scales; ``router_w`` fp32 [E, H], ``router_bias`` [E].  With ``ep_group``
     (a torch.distributed process group) the weights passed are this rank's
     E/world experts and tokens are exchanged with NCCL all-to-all.
-    ``logits`` overrides the router GEMM.
+    ``logits`` overrides the router GEMM.  ``profile_events`` (three recorded
+    ``torch.cuda.Event``) brackets GEMM1 and GEMM2 for kernel timing.
     """
     if ep_group is not None:
         from . import ep
@@ -236,7 +237,12 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
         counts = torch.empty((E,), dtype=torch.int32, device=dev)
         args.topk_idx_out, args.topk_w_out, args.expert_counts_out = _ptr(idx), _ptr(w), _ptr(counts)
+    ev_arr = None
+    if profile_events is not None:
+        ev_arr = (ctypes.c_void_p * 3)(*[e.cuda_event for e in profile_events])
+        args.profile_events = ctypes.cast(ev_arr, ctypes.c_void_p)
     _call_fwd(shape, args, dev, "moe")
+    del ev_arr
     if return_routing:
         return out, idx, w, counts, logits
     return out

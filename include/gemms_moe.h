@@ -83,6 +83,9 @@ typedef struct {
   int32_t* topk_idx_out;            /* optional int32 [T, top_k] (NULL: skip)      */
   float* topk_w_out;                /* optional fp32 [T, top_k]                    */
   int32_t* expert_counts_out;       /* optional int32 [E_local]                    */
+  void* const* profile_events;      /* optional: 3 cudaEvent_t recorded on the     */
+                                    /* stream before GEMM1, between GEMM1 and      */
+                                    /* GEMM2, and after GEMM2 (kernel timing)      */
 } GemmsMoeArgs;
 
 /* Bytes of device workspace gemms_moe_fwd needs for this shape. */
