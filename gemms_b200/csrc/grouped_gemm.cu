@@ -28,6 +28,7 @@
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 
 namespace gemms {
@@ -38,8 +39,21 @@ constexpr int BM = 128;                 // rows per tile = TMEM lanes
 constexpr int BN = 256;                 // output columns per tile
 constexpr int BK = 128;                 // K (bytes) per stage = one scale block
 constexpr int UMMA_K = 32;              // K per tcgen05.mma for 8-bit inputs
-constexpr int kThreads = 320;
-constexpr int kEpiWarps = 8;
+constexpr int kThreads = 384;          // 3 warpgroups
+constexpr int kEpiWarps = 8;           // warpgroups 1-2
+constexpr int kEpiFirstWarp = 4;
+// Register split (setmaxnreg): launched at 168/thread (384 threads), the
+// producer/MMA warpgroup drops to `ctrl` and the two epilogue warpgroups rise
+// to `epi`, with ctrl + 2 x epi <= 504 <= 512 registers per lane of an SM
+// sub-partition and 4x32xctrl + 8x32xepi <= 64512 = 384 x 168 (the launch
+// allocation).  The epilogue share holds the 128 running sums plus two
+// 32-column TMEM loads per wait without spilling.
+// GEMM1's epilogue (SwiGLU + requant) needs the larger share; GEMM2's
+// producer needs more than 40.  Both splits satisfy the budgets above.
+template <int MODE> struct Regs {
+  static constexpr int ctrl = MODE == 0 ? 40 : 56;
+  static constexpr int epi = MODE == 0 ? 232 : 224;
+};
 constexpr uint32_t kTmemCols = 512;     // 2 partial accumulators x 256 columns
 constexpr int kTileA = BM * BK;         // 16 KB
 constexpr int kTileB = BN * BK;         // 32 KB
@@ -65,6 +79,7 @@ struct GemmParams {
   int w_rows;        // weight rows per expert
   int b_row_step;    // weight rows per N tile step
   int b_row_hi;      // row offset of the second 128-row weight box
+  int prefetch;      // weight K-blocks prefetched into L2 ahead of the smem ring
   const float* a_scale;
   int a_scale_ld;
   const float* w_scale;   // [E, w_rows/128, kb_count]
@@ -146,11 +161,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = min(*p.num_tiles, p.max_tiles);
   const int total = num_tiles * p.n_tiles;
 
-  if (warp == 0) {
+  if (warp < kEpiFirstWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(Regs<MODE>::ctrl));
+   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
+      // Weight coordinates of this CTA's it-th K iteration (units are strided
+      // by gridDim.x); used both to load and to prefetch ahead into L2.
+      const int my_units = total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+      const int my_iters = my_units * p.kb_count;
+      auto weight_rows = [&](int it, int& kb, int& wrow, const CUtensorMap*& mb) {
+        const int i = it / p.kb_count;
+        kb = it - i * p.kb_count;
+        const int u = blockIdx.x + i * gridDim.x;
+        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        const int g = p.tile_group[mt];
+        const bool sh = (g == p.shared_group);
+        mb = sh ? &tmBs : &tmB;
+        wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
+      };
+      for (int pf = 0; pf < p.prefetch && pf < my_iters; ++pf) {
+        int kb, wrow;
+        const CUtensorMap* mb;
+        weight_rows(pf, kb, wrow, mb);
+        tma_prefetch_l2_2d(mb, kb * BK, wrow, pol_w);
+        tma_prefetch_l2_2d(mb, kb * BK, wrow + p.b_row_hi, pol_w);
+      }
       int it = 0;
       for (int u = blockIdx.x; u < total; u += gridDim.x) {
         const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
@@ -162,6 +200,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
+          if (p.prefetch > 0 && it + p.prefetch < my_iters) {
+            int pkb, pwrow;
+            const CUtensorMap* pmb;
+            weight_rows(it + p.prefetch, pkb, pwrow, pmb);
+            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow, pol_w);
+            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow + p.b_row_hi, pol_w);
+          }
           if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
             ok = false;
             break;
@@ -183,10 +228,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_drain(&full[s], (last / S) & 1);
       }
     }
-  } else if (warp == 1) {
+   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+      // Descriptors of every stage's operand tiles, computed once: a K step
+      // of 32 bytes inside the 128-byte swizzle row adds 2 (16-byte units) to
+      // the start-address field.  Keeps this thread's per-K-block issue short;
+      // it shares an SM sub-partition with two epilogue warps.
+      uint64_t da[S][PLANES], db[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        uint8_t* st = smem + s * C::kStageBytes;
+#pragma unroll
+        for (int pl = 0; pl < PLANES; ++pl) da[s][pl] = smem_desc_k_sw128(smem_u32(st + pl * kTileA));
+        db[s] = smem_desc_k_sw128(smem_u32(st + PLANES * kTileA));
+      }
       int it = 0, acc_it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
@@ -203,15 +260,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t d = tmem_base + buf * BN;
-          uint8_t* st = smem + s * C::kStageBytes;
-          const uint32_t b_addr = smem_u32(st + PLANES * kTileA);
+          uint64_t bd = db[0];
+          uint64_t ad[PLANES];
+#pragma unroll
+          for (int ss = 0; ss < S; ++ss)
+            if (ss == s) {
+              bd = db[ss];
+#pragma unroll
+              for (int pl = 0; pl < PLANES; ++pl) ad[pl] = da[ss][pl];
+            }
 #pragma unroll
           for (int pl = 0; pl < PLANES; ++pl) {
-            const uint32_t a_addr = smem_u32(st + pl * kTileA);
 #pragma unroll
             for (int ks = 0; ks < BK / UMMA_K; ++ks)
-              umma_f8f6f4(d, smem_desc_k_sw128(a_addr + ks * UMMA_K), smem_desc_k_sw128(b_addr + ks * UMMA_K),
-                          idesc, (pl | ks) != 0);
+              umma_f8f6f4(d, ad[pl] + 2 * ks, bd + 2 * ks, idesc, (pl | ks) != 0);
           }
           umma_commit(&empty[s]);
           umma_commit(&pfull[buf]);
@@ -222,9 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
     }
+   }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(Regs<MODE>::epi));
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;
+    const int ew = warp - kEpiFirstWarp;
     const int q = warp & 3;         // TMEM lane quadrant this warp may access
     const int h = ew >> 2;          // column half
     const int r = q * 32 + lane;    // row within the tile
@@ -245,43 +309,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         blk0 = blk1 = 2 * nt + h;           // output columns [nt*256 + 128h, +128)
       }
-      const float* a_sc = p.a_scale + row0 + r;
+      // Scales are prefetched three K blocks ahead (global-load latency is
+      // ~1 pipeline iteration under load).  Rows past the tile's valid count
+      // read row 0's scale and are never stored.
+      const float* a_sc = p.a_scale + row0 + (valid ? r : 0);
+      const float* w0p = ws + (size_t)blk0 * p.kb_count;
+      const float* w1p = ws + (size_t)blk1 * p.kb_count;
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
-      float as_n = valid ? __ldg(a_sc) : 0.f;
-      float w0_n = __ldg(ws + (size_t)blk0 * p.kb_count);
-      float w1_n = __ldg(ws + (size_t)blk1 * p.kb_count);
-      for (int kb = 0; kb < p.kb_count; ++kb, ++acc_it) {
-        const float f0 = as_n * w0_n, f1 = as_n * w1_n;
-        if (kb + 1 < p.kb_count) {  // prefetch next block's scales
-          as_n = valid ? __ldg(a_sc + (size_t)(kb + 1) * p.a_scale_ld) : 0.f;
-          w0_n = __ldg(ws + (size_t)blk0 * p.kb_count + kb + 1);
-          w1_n = __ldg(ws + (size_t)blk1 * p.kb_count + kb + 1);
+      const int KB = p.kb_count;
+      float as0 = __ldg(a_sc), w00 = __ldg(w0p), w10 = __ldg(w1p);
+      float as1 = 0.f, w01 = 0.f, w11 = 0.f, as2 = 0.f, w02 = 0.f, w12 = 0.f;
+      if (KB > 1) {
+        as1 = __ldg(a_sc + (size_t)p.a_scale_ld);
+        w01 = __ldg(w0p + 1);
+        w11 = __ldg(w1p + 1);
+      }
+      if (KB > 2) {
+        as2 = __ldg(a_sc + 2 * (size_t)p.a_scale_ld);
+        w02 = __ldg(w0p + 2);
+        w12 = __ldg(w1p + 2);
+      }
+      for (int kb = 0; kb < KB; ++kb, ++acc_it) {
+        const float f0 = as0 * w00, f1 = as0 * w10;
+        as0 = as1; w00 = w01; w10 = w11;
+        as1 = as2; w01 = w02; w11 = w12;
+        if (kb + 3 < KB) {
+          as2 = __ldg(a_sc + (size_t)(kb + 3) * p.a_scale_ld);
+          w02 = __ldg(w0p + kb + 3);
+          w12 = __ldg(w1p + kb + 3);
         }
         const int buf = acc_it & 1;
-        if (!mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait)) {
+        // One lane polls the barrier; the warp waits at __syncwarp.
+        int got = 1;
+        if (lane == 0) got = mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        __syncwarp();
+        if (!got) {
           ok = false;
           break;
         }
-        __syncwarp();
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          int col;
-          float f;
+        for (int c = 0; c < 4; c += 2) {
+          int col0, col1;
+          float fa, fb;
           if (MODE == 0) {
-            col = (c < 2) ? (64 * h + 32 * c) : (128 + 64 * h + 32 * (c - 2));
-            f = (c < 2) ? f0 : f1;
+            // gate columns (c = 0, 1) then up columns (c = 2, 3)
+            col0 = (c < 2) ? (64 * h + 32 * c) : (128 + 64 * h + 32 * (c - 2));
+            col1 = col0 + 32;
+            fa = fb = (c < 2) ? f0 : f1;
           } else {
-            col = 128 * h + 32 * c;
-            f = f0;
+            col0 = 128 * h + 32 * c;
+            col1 = col0 + 32;
+            fa = fb = f0;
           }
-          float v[32];
-          tmem_ld_32x32b_x32(lane_base + buf * BN + col, v);
+          float v0[32], v1[32];
+          tmem_ld_32x32b_x32(lane_base + buf * BN + col0, v0);
+          tmem_ld_32x32b_x32(lane_base + buf * BN + col1, v1);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[32 * c + i] = fmaf(f, v[i], acc[32 * c + i]);
+          for (int i = 0; i < 32; i += 2) {
+            ffma2(acc[32 * c + i], acc[32 * c + i + 1], fa, v0[i], v0[i + 1]);
+            ffma2(acc[32 * c + 32 + i], acc[32 * c + 33 + i], fb, v1[i], v1[i + 1]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -356,6 +448,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
+// Weight K-blocks a CTA keeps in flight toward L2 beyond its smem ring.  The
+// weight stream is DRAM-latency bound (one 32 KB stage per K-block per SM);
+// GEMMS_PREFETCH overrides the default for tuning.
+int prefetch_depth() {
+  static int depth = -1;
+  if (depth < 0) {
+    const char* e = getenv("GEMMS_PREFETCH");
+    depth = e ? atoi(e) : 0;
+    if (depth < 0) depth = 0;
+    if (depth > 64) depth = 64;
+  }
+  return depth;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -427,6 +533,7 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.w_rows = 2 * a.I;
   p.b_row_step = kBlock;
   p.b_row_hi = a.I;
+  p.prefetch = prefetch_depth();
   p.a_scale = a.a_scale;
   p.a_scale_ld = a.a_scale_ld;
   p.w_scale = a.w13_scale;
@@ -467,6 +574,7 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.w_rows = a.H;
   p.b_row_step = BN;
   p.b_row_hi = kBlock;
+  p.prefetch = prefetch_depth();
   p.a_scale = a.inter_scale;
   p.a_scale_ld = a.inter_scale_ld;
   p.w_scale = a.w2_scale;

@@ -6,18 +6,23 @@
 // Replaces the reference's blackwell.h, whose smem descriptor lacks the
 // version field and whose tcgen05 forms do not assemble for sm_100a.
 //
-// Every wait is bounded: a spin that exceeds GEMMS_WAIT_TIMEOUT_NS sets a bit
+// Every wait is bounded: a spin that exceeds time limit (clock64 cycles for pipeline waits) sets a bit
 // in a device error word and raises a CTA-wide abort flag instead of hanging.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
 
 #ifndef GEMMS_WAIT_TIMEOUT_NS
-#define GEMMS_WAIT_TIMEOUT_NS 4000000000ull  // 4 s
+#define GEMMS_WAIT_TIMEOUT_NS 4000000000ull  // 4 s (drain waits, %globaltimer)
+#endif
+#ifndef GEMMS_WAIT_TIMEOUT_CYCLES
+#define GEMMS_WAIT_TIMEOUT_CYCLES 8000000000ll  // ~4 s at 2 GHz (pipeline waits, clock64)
 #endif
 
 namespace gemms {
 namespace sm100 {
+
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms; waiters resume on phase completion
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -47,36 +52,42 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or the hint expires) instead of spinning, leaving issue slots to
+// the warps that share its SM sub-partition.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
 // Waits for the phase with `parity` to complete.  Returns false (after
 // setting *abort and OR-ing `code` into *err) when the wait exceeds the
-// timeout, or as soon as another role has raised *abort.
+// timeout, or as soon as another role has raised *abort.  The timeout runs on
+// the SM cycle counter (cheap to read), checked every 256 polls; reading
+// %globaltimer on every miss added ~1 us to each pipeline hand-off.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > GEMMS_WAIT_TIMEOUT_NS) {
-      *abort_flag = 1;
-      atomicOr(err, code);
-      return false;
+  const long long t0 = clock64();
+  uint32_t n = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++n & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > GEMMS_WAIT_TIMEOUT_CYCLES) {
+        *abort_flag = 1;
+        atomicOr(err, code);
+        return false;
+      }
     }
   }
+  return true;
 }
 
 // Named barrier over `nthreads` threads (ids 1..15; 0 is __syncthreads).
@@ -109,6 +120,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Prefetch a 2-D tile into L2 (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 
@@ -167,6 +187,18 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// (a0, a1) += f * (v0, v1) as one packed fp32x2 FMA (sm_100 f32x2 pipe).
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float f, float v0, float v1) {
+  asm("{\n\t.reg .b64 acc, fv, vv;\n\t"
+      "mov.b64 acc, {%0, %1};\n\t"
+      "mov.b64 fv, {%2, %2};\n\t"
+      "mov.b64 vv, {%3, %4};\n\t"
+      "fma.rn.f32x2 acc, fv, vv, acc;\n\t"
+      "mov.b64 {%0, %1}, acc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(f), "f"(v0), "f"(v1));
+}
 
 // ------------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte
