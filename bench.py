@@ -310,11 +310,16 @@ def gpu_arm(a):
               inter_planes=planes, ep_group=group, **shared_kw)
 
     def step(x, events=None):
-        if group is None:
+        # NVTX range per step: `ncu --nvtx --nvtx-include moe_step/` selects the layer's launches.
+        torch.cuda.nvtx.range_push("moe_step")
+        try:
+            if group is None:
+                return gemms_b200.moe(x, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                                      d["w2_scale"], profile_events=events, **kw)
             return gemms_b200.moe(x, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
-                                  d["w2_scale"], profile_events=events, **kw)
-        return gemms_b200.moe(x, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
-                              d["w2_scale"], **kw)
+                                  d["w2_scale"], **kw)
+        finally:
+            torch.cuda.nvtx.range_pop()
 
     def barrier():
         if group is not None:
