@@ -97,6 +97,19 @@ size_t gemms_moe_workspace_size(const GemmsMoeShape* shape);
  * initialisation.  Concurrent calls need distinct workspaces. */
 int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, gemms_stream_t stream);
 
+/* gemms_moe_fwd without a caller workspace, for callers that cannot allocate
+ * device memory where they run the layer (plugin hosts that provide a stream
+ * but no allocator, runtimes that forbid allocations once serving starts).
+ * No counterpart in the reference.  Scratch is a fixed 16 MiB device array
+ * inside this library, held by every GPU that loads it until process exit;
+ * shapes whose gemms_moe_workspace_size() exceeds 16 MiB are rejected with
+ * GEMMS_ERR_CAPACITY (DeepSeek-V3 shapes with a shared expert: up to 126
+ * tokens).  The first call on a device looks up the array's device address
+ * (make it before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU (other streams, other host threads) race.  Allocates
+ * nothing. */
+int gemms_moe_fwd_noalloc(const GemmsMoeArgs* args, gemms_stream_t stream);
+
 /* Router only (for tests and expert-parallel dispatch): fp32 logits [T,E] +
  * bias -> topk_idx int32 [T,top_k] (descending biased score), topk_w fp32
  * [T,top_k] (normalised, times the scaling factor), and counts int32 [E]
