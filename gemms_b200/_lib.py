@@ -29,6 +29,11 @@ EXPORTS = (
     "gemms_moe_check",
     "gemms_strerror",
     "gemms_version",
+    "gemms_ep_row_bytes",
+    "gemms_ep_dispatch",
+    "gemms_ep_ffn_workspace_size",
+    "gemms_ep_expert_ffn",
+    "gemms_ep_combine",
 )
 
 
@@ -103,6 +108,19 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_strerror.restype = ctypes.c_char_p
         L.gemms_version.argtypes = []
         L.gemms_version.restype = ctypes.c_char_p
+        L.gemms_ep_row_bytes.argtypes = [c_int32, c_int32]
+        L.gemms_ep_row_bytes.restype = c_size_t
+        L.gemms_ep_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+        L.gemms_ep_dispatch.restype = c_int32
+        L.gemms_ep_ffn_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]
+        L.gemms_ep_ffn_workspace_size.restype = c_size_t
+        L.gemms_ep_expert_ffn.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                          c_void_p]
+        L.gemms_ep_expert_ffn.restype = c_int32
+        L.gemms_ep_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
+        L.gemms_ep_combine.restype = c_int32
         _lib = L
         return L
 

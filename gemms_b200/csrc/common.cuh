@@ -69,6 +69,7 @@ struct AssignArgs {
   const int32_t* topk_idx;
   const float* topk_w;
   int T, top_k, local_offset, E_local;
+  int idx_stride;          // elements between consecutive tokens' ids / weights (0: top_k)
   const int32_t* offsets;
   int32_t* row_token;     // [rows]
   float* row_weight;      // [rows]
@@ -83,8 +84,11 @@ struct PermuteArgs {
   int mode;                        // GEMMS_INPUT_BF16 / GEMMS_INPUT_FP8
   const __nv_bfloat16* x_bf16;     // [T, H]
   const uint8_t* x_fp8;            // [T, H]
-  const float* x_scale;            // [H/128, T]
+  const float* x_scale;            // [H/128, T] (or strided, see below)
   int T, H, top_k;
+  long long x_row_stride;          // bytes between fp8 input rows (0: H)
+  long long scale_kb_stride;       // floats between 128-column blocks of x_scale (0: T)
+  long long scale_t_stride;        // floats between tokens of x_scale (0: 1)
   const int32_t* pair_row;         // [T, top_k] (-1 = not local)
   const int32_t* shared_row0;      // device int (nullptr: none); token t also goes to row *shared_row0 + t
   uint8_t* rows_fp8;

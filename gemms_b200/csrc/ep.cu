@@ -1,0 +1,425 @@
+// ep.cu -- expert-parallel dispatch / receive-side expert FFN / combine.
+//
+// The reference has no distributed path: its only hook is local_expert_offset
+// (flashinfer_baseline.py:132-138, persistent_kernel2.cu:332).  Rank r owns
+// experts [r*E_local, (r+1)*E_local); these kernels build the exchange around
+// that convention (the all-to-alls themselves are NCCL calls issued by the
+// host, gemms_b200/ep.py):
+//
+//   dispatch  : per token, the set of destination ranks holding any of its
+//               top-k experts (each token goes once to each such rank); rows
+//               are laid out grouped by destination in increasing token order
+//               (deterministic).  The token is quantised per 1x128 once and
+//               packed with its scales and the ids/weights of the experts
+//               that live on the destination.  Also writes the token-major
+//               quantised rows used by the local shared expert.
+//   expert ffn: the packed received rows, read in place (strided), go through
+//               histogram -> plan -> assign -> permute -> GEMM1 -> GEMM2; each
+//               received row's result is pre-reduced over its local experts in
+//               fp32.
+//   combine   : out[t] = bf16(acc[t] + sum over t's destinations of the rows
+//               sent back), gathered deterministically.
+//
+// Packed row layout (row_bytes = align16(H + 4*H/128 + 8*top_k)):
+//   [0, H)                    e4m3 activations
+//   [H, H + 4*H/128)          fp32 1x128 scales
+//   [.., + 4*top_k)           int32 global expert ids on the destination, -1 padded
+//   [.., + 4*top_k)           fp32 routing weights
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace gemms {
+namespace {
+
+constexpr int kMaxWorld = 32;
+
+__host__ __device__ inline size_t ep_row_bytes(int H, int top_k) {
+  return align_up((size_t)H + 4 * (size_t)(H / kBlock) + 8 * (size_t)top_k, 16);
+}
+
+__device__ __forceinline__ unsigned dest_mask(const int32_t* idx, int top_k, int E_local) {
+  unsigned m = 0;
+  for (int j = 0; j < top_k; ++j) {
+    const int e = idx[j];
+    if (e >= 0) m |= 1u << (e / E_local);
+  }
+  return m;
+}
+
+// Thread per token: per-destination row counts.
+__global__ void ep_count_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k, int E_local,
+                                int32_t* __restrict__ send_counts) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  unsigned m = dest_mask(topk_idx + (size_t)t * top_k, top_k, E_local);
+  while (m) {
+    const int d = __ffs(m) - 1;
+    m &= m - 1;
+    atomicAdd(send_counts + d, 1);
+  }
+}
+
+// Block per destination: send rows in increasing token order.
+__global__ void __launch_bounds__(1024) ep_assign_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k,
+                                                         int E_local, int world,
+                                                         const int32_t* __restrict__ send_counts,
+                                                         int32_t* __restrict__ send_row_of) {
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  const int d = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  if (tid == 0) {
+    int o = 0;
+    for (int i = 0; i < d; ++i) o += send_counts[i];
+    s_base = o;
+  }
+  __syncthreads();
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + tid;
+    bool f = false;
+    if (t < T) f = (dest_mask(topk_idx + (size_t)t * top_k, top_k, E_local) >> d) & 1u;
+    const unsigned ballot = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) s_warp[warp] = __popc(ballot);
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < nwarps ? s_warp[lane] : 0;
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+      }
+      if (lane < nwarps) s_warp[lane] = v;
+    }
+    __syncthreads();
+    const int base = s_base;
+    if (t < T) {
+      send_row_of[(size_t)t * world + d] =
+          f ? base + (warp > 0 ? s_warp[warp - 1] : 0) + __popc(ballot & ((1u << lane) - 1u)) : -1;
+    }
+    __syncthreads();
+    if (tid == 0) s_base = base + s_warp[nwarps - 1];
+    __syncthreads();
+  }
+}
+
+// Block (8 warps) per token: quantise once, write the token-major rows and
+// every packed send row of the token.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      const int32_t* __restrict__ topk_idx,
+                                                      const float* __restrict__ topk_w, int T, int H, int top_k,
+                                                      int E_local, int world,
+                                                      const int32_t* __restrict__ send_row_of,
+                                                      uint8_t* __restrict__ send_buf, size_t row_bytes,
+                                                      uint8_t* __restrict__ xq, float* __restrict__ xq_scale) {
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int rows[kMaxWorld];
+  int dests[kMaxWorld];
+  int nd = 0;
+  for (int d = 0; d < world; ++d) {
+    const int r = send_row_of[(size_t)t * world + d];
+    if (r >= 0) {
+      rows[nd] = r;
+      dests[nd] = d;
+      ++nd;
+    }
+  }
+  const int KB = H / kBlock;
+  for (int kb = warp; kb < KB; kb += 8) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + (size_t)t * H + (size_t)kb * kBlock + lane * 4);
+    const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    const float v0 = __low2float(p0), v1 = __high2float(p0), v2 = __low2float(p1), v3 = __high2float(p1);
+    float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+    const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fdiv_rn(v0, scale), __fdiv_rn(v1, scale)), __NV_SATFINITE, __NV_E4M3);
+    const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fdiv_rn(v2, scale), __fdiv_rn(v3, scale)), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t packed = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    *reinterpret_cast<uint32_t*>(xq + (size_t)t * H + (size_t)kb * kBlock + lane * 4) = packed;
+    if (lane == 0) xq_scale[(size_t)kb * T + t] = scale;
+    for (int i = 0; i < nd; ++i) {
+      uint8_t* row = send_buf + (size_t)rows[i] * row_bytes;
+      *reinterpret_cast<uint32_t*>(row + (size_t)kb * kBlock + lane * 4) = packed;
+      if (lane == 0) reinterpret_cast<float*>(row + H)[kb] = scale;
+    }
+  }
+  // expert ids / weights that live on each destination
+  if (warp == 0) {
+    for (int i = 0; i < nd; ++i) {
+      uint8_t* row = send_buf + (size_t)rows[i] * row_bytes;
+      int32_t* ids = reinterpret_cast<int32_t*>(row + H + 4 * KB);
+      float* ws = reinterpret_cast<float*>(row + H + 4 * KB + 4 * top_k);
+      for (int j = lane; j < top_k; j += 32) {
+        const int e = topk_idx[(size_t)t * top_k + j];
+        const bool here = e >= 0 && e / E_local == dests[i];
+        ids[j] = here ? e : -1;
+        ws[j] = here ? topk_w[(size_t)t * top_k + j] : 0.f;
+      }
+    }
+  }
+}
+
+// Thread per received row: local-expert histogram and pair_row = -1.
+__global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R, int H, int top_k,
+                               int local_offset, int E_local, int32_t* __restrict__ counts,
+                               int32_t* __restrict__ pair_row, int* err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  const int32_t* ids = reinterpret_cast<const int32_t*>(recv + (size_t)r * row_bytes + H + 4 * (H / kBlock));
+  for (int j = 0; j < top_k; ++j) {
+    pair_row[(size_t)r * top_k + j] = -1;
+    const int e = ids[j];
+    if (e < 0) continue;
+    const int le = e - local_offset;
+    if (le >= 0 && le < E_local)
+      atomicAdd(counts + le, 1);
+    else
+      atomicOr(err, kErrBadExpertIndex);
+  }
+}
+
+// Block per token: out[t] = bf16(acc[t] + sum of the token's returned rows).
+__global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc,
+                                                         const float* __restrict__ back,
+                                                         const int32_t* __restrict__ send_row_of, int T, int H,
+                                                         int world, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  int rows[kMaxWorld];
+  int nd = 0;
+  for (int d = 0; d < world; ++d) {
+    const int r = send_row_of[(size_t)t * world + d];
+    if (r >= 0) rows[nd++] = r;
+  }
+  for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
+    float4 s = *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
+    for (int i = 0; i < nd; ++i) {
+      const float4 b = *reinterpret_cast<const float4*>(back + (size_t)rows[i] * H + c);
+      s.x += b.x;
+      s.y += b.y;
+      s.z += b.z;
+      s.w += b.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&lo);
+    o.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(out + (size_t)t * H + c) = o;
+  }
+}
+
+struct EpFfnLayout {
+  int groups, max_tiles, scale_ld;
+  size_t err, counts, offsets, tile_group, tile_row0, tile_rows, num_tiles, pair_row, row_token, row_weight;
+  size_t a_rows, a_scale, inter, inter_scale, total, head;
+};
+
+EpFfnLayout ep_ffn_layout(int R_max, int H, int I, int E_local, int top_k, int planes) {
+  EpFfnLayout L{};
+  const int P = std::max(R_max * top_k, 1);  // grouped pair rows
+  L.groups = E_local;
+  L.max_tiles = cdiv(P, kBlock) + E_local;
+  L.scale_ld = static_cast<int>(align_up(P, 32));
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  L.err = take(64);
+  L.counts = take(sizeof(int32_t) * std::max(E_local, 1));
+  L.head = o;
+  L.offsets = take(sizeof(int32_t) * (E_local + 1));
+  L.tile_group = take(sizeof(int32_t) * L.max_tiles);
+  L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
+  L.tile_rows = take(sizeof(int32_t) * L.max_tiles);
+  L.num_tiles = take(sizeof(int32_t));
+  L.pair_row = take(sizeof(int32_t) * (size_t)std::max(R_max, 1) * top_k);
+  L.row_token = take(sizeof(int32_t) * P);
+  L.row_weight = take(sizeof(float) * P);
+  L.a_rows = take((size_t)P * H);
+  L.a_scale = take(sizeof(float) * (size_t)(H / kBlock) * L.scale_ld);
+  L.inter = take((size_t)P * planes * I);
+  L.inter_scale = take(sizeof(float) * (size_t)(I / kBlock) * L.scale_ld);
+  L.total = o;
+  return L;
+}
+
+template <class T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+}  // namespace
+}  // namespace gemms
+
+using namespace gemms;
+
+extern "C" {
+
+size_t gemms_ep_row_bytes(int32_t H, int32_t top_k) { return ep_row_bytes(H, top_k); }
+
+int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* x_bf16, int32_t T, int32_t H,
+                      int32_t top_k, int32_t world, int32_t E_local, int32_t* send_counts, int32_t* send_row_of,
+                      void* send_buf, void* xq, float* xq_scale, gemms_stream_t stream_) {
+  if (T < 0 || H <= 0 || H % kBlock || top_k < 1 || top_k > 16 || world < 1 || world > kMaxWorld || E_local < 1)
+    return GEMMS_ERR_SHAPE;
+  if (!topk_idx || !topk_w || !x_bf16 || !send_counts || !send_row_of || !send_buf || !xq || !xq_scale)
+    return GEMMS_ERR_ARG;
+  if (!aligned16(send_buf) || !aligned16(xq) || !aligned16(x_bf16)) return GEMMS_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+  GEMMS_CUDA_TRY(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, st));
+  if (T == 0) return GEMMS_OK;
+  ep_count_kernel<<<cdiv(T, 256), 256, 0, st>>>(topk_idx, T, top_k, E_local, send_counts);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  ep_assign_kernel<<<world, 1024, 0, st>>>(topk_idx, T, top_k, E_local, world, send_counts, send_row_of);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  ep_pack_kernel<<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x_bf16), topk_idx, topk_w, T, H, top_k,
+                                     E_local, world, send_row_of, static_cast<uint8_t*>(send_buf),
+                                     ep_row_bytes(H, top_k), static_cast<uint8_t*>(xq), xq_scale);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t H, int32_t I, int32_t E_local, int32_t top_k,
+                                   int32_t inter_planes) {
+  const int planes = inter_planes == 0 ? 2 : inter_planes;
+  if (R_max < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
+      planes < 2 || planes > 3)
+    return 0;
+  return ep_ffn_layout(R_max, H, I, E_local, top_k, planes).total;
+}
+
+int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, int32_t top_k, int32_t E_local,
+                        int32_t local_expert_offset, int32_t inter_planes, const void* w13, const float* w13_scale,
+                        const void* w2, const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
+                        gemms_stream_t stream_) {
+  const int planes = inter_planes == 0 ? 2 : inter_planes;
+  if (R < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
+      planes < 2 || planes > 3)
+    return GEMMS_ERR_SHAPE;
+  if (!recv_buf || !w13 || !w13_scale || !w2 || !w2_scale || !out_rows) return GEMMS_ERR_ARG;
+  const EpFfnLayout L = ep_ffn_layout(R, H, I, E_local, top_k, planes);
+  if (!workspace || ws_bytes < L.total) return GEMMS_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GEMMS_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+  if (R == 0) return GEMMS_OK;
+  void* ws = workspace;
+  int* err = at<int>(ws, L.err);
+  const size_t rb = ep_row_bytes(H, top_k);
+  const uint8_t* recv = static_cast<const uint8_t*>(recv_buf);
+  GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, L.head, st));
+  GEMMS_CUDA_TRY(cudaMemsetAsync(out_rows, 0, sizeof(float) * (size_t)R * H, st));
+  int32_t* pair_row = at<int32_t>(ws, L.pair_row);
+  ep_hist_kernel<<<cdiv(R, 256), 256, 0, st>>>(recv, rb, R, H, top_k, local_expert_offset, E_local,
+                                                at<int32_t>(ws, L.counts), pair_row, err);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  int rc;
+  PlanArgs pa{};
+  pa.counts = at<int32_t>(ws, L.counts);
+  pa.E_local = E_local;
+  pa.shared_rows = 0;
+  pa.offsets = at<int32_t>(ws, L.offsets);
+  pa.tile_group = at<int32_t>(ws, L.tile_group);
+  pa.tile_row0 = at<int32_t>(ws, L.tile_row0);
+  pa.tile_rows = at<int32_t>(ws, L.tile_rows);
+  pa.num_tiles = at<int32_t>(ws, L.num_tiles);
+  pa.max_tiles = L.max_tiles;
+  pa.err = err;
+  if ((rc = launch_plan(pa, st))) return rc;
+
+  const int KB = H / kBlock;
+  AssignArgs sa{};
+  sa.topk_idx = reinterpret_cast<const int32_t*>(recv + H + 4 * KB);
+  sa.topk_w = reinterpret_cast<const float*>(recv + H + 4 * KB + 4 * top_k);
+  sa.idx_stride = static_cast<int>(rb / 4);
+  sa.T = R;
+  sa.top_k = top_k;
+  sa.local_offset = local_expert_offset;
+  sa.E_local = E_local;
+  sa.offsets = pa.offsets;
+  sa.row_token = at<int32_t>(ws, L.row_token);
+  sa.row_weight = at<float>(ws, L.row_weight);
+  sa.pair_row = pair_row;
+  sa.shared_rows = 0;
+  if ((rc = launch_assign(sa, st))) return rc;
+
+  PermuteArgs qa{};
+  qa.mode = GEMMS_INPUT_FP8;
+  qa.x_fp8 = recv;
+  qa.x_scale = reinterpret_cast<const float*>(recv + H);
+  qa.x_row_stride = static_cast<long long>(rb);
+  qa.scale_kb_stride = 1;
+  qa.scale_t_stride = static_cast<long long>(rb / 4);
+  qa.T = R;
+  qa.H = H;
+  qa.top_k = top_k;
+  qa.pair_row = pair_row;
+  qa.shared_row0 = nullptr;
+  qa.rows_fp8 = at<uint8_t>(ws, L.a_rows);
+  qa.rows_scale = at<float>(ws, L.a_scale);
+  qa.scale_ld = L.scale_ld;
+  if ((rc = launch_permute(qa, st))) return rc;
+
+  GemmGroupsArgs gg{};
+  gg.tile_group = pa.tile_group;
+  gg.tile_row0 = pa.tile_row0;
+  gg.tile_rows = pa.tile_rows;
+  gg.num_tiles = pa.num_tiles;
+  gg.max_tiles = L.max_tiles;
+  gg.shared_group = -1;
+  const int P = std::max(R * top_k, 1);
+
+  Gemm1Args g1{};
+  g1.g = gg;
+  g1.a = qa.rows_fp8;
+  g1.a_rows = P;
+  g1.a_scale = qa.rows_scale;
+  g1.a_scale_ld = L.scale_ld;
+  g1.w13 = static_cast<const uint8_t*>(w13);
+  g1.w13_scale = w13_scale;
+  g1.E_local = E_local;
+  g1.H = H;
+  g1.I = I;
+  g1.planes = planes;
+  g1.inter = at<uint8_t>(ws, L.inter);
+  g1.inter_scale = at<float>(ws, L.inter_scale);
+  g1.inter_scale_ld = L.scale_ld;
+  g1.err = err;
+  if ((rc = launch_gemm1(g1, st))) return rc;
+
+  Gemm2Args g2{};
+  g2.g = gg;
+  g2.inter = g1.inter;
+  g2.a_rows = P;
+  g2.inter_scale = g1.inter_scale;
+  g2.inter_scale_ld = L.scale_ld;
+  g2.w2 = static_cast<const uint8_t*>(w2);
+  g2.w2_scale = w2_scale;
+  g2.E_local = E_local;
+  g2.H = H;
+  g2.I = I;
+  g2.planes = planes;
+  g2.row_dest = sa.row_token;
+  g2.row_weight = sa.row_weight;
+  g2.out = out_rows;
+  g2.err = err;
+  return launch_gemm2(g2, st);
+}
+
+int gemms_ep_combine(const float* acc, const float* back_rows, const int32_t* send_row_of, int32_t T, int32_t H,
+                     int32_t world, void* out_bf16, gemms_stream_t stream_) {
+  if (T < 0 || H <= 0 || H % 4 || world < 1 || world > kMaxWorld) return GEMMS_ERR_SHAPE;
+  if (!acc || !send_row_of || !out_bf16) return GEMMS_ERR_ARG;  // back_rows may be NULL when nothing was sent
+  if (!aligned16(acc) || !aligned16(out_bf16) || (back_rows && !aligned16(back_rows))) return GEMMS_ERR_ALIGN;
+  if (T == 0) return GEMMS_OK;
+  ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      acc, back_rows, send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+}  // extern "C"

@@ -52,8 +52,11 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a) {
       scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
       packed = quant4(v0, v1, v2, v3, scale);
     } else {
-      packed = *reinterpret_cast<const uint32_t*>(a.x_fp8 + src);
-      scale = a.x_scale[(size_t)kb * a.T + t];
+      const long long rs = a.x_row_stride > 0 ? a.x_row_stride : a.H;
+      const long long skb = a.scale_kb_stride > 0 ? a.scale_kb_stride : a.T;
+      const long long st = a.scale_t_stride > 0 ? a.scale_t_stride : 1;
+      packed = *reinterpret_cast<const uint32_t*>(a.x_fp8 + (size_t)t * rs + (size_t)kb * kBlock + lane * 4);
+      scale = a.x_scale[kb * skb + t * st];
     }
     for (int d = 0; d < nd; ++d) {
       const int r = dst[d];

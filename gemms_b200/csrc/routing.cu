@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
     return;
   }
   const int ge = a.local_offset + le;
+  const int stride = a.idx_stride > 0 ? a.idx_stride : a.top_k;
   if (tid == 0) s_base = a.offsets[le];
   __syncthreads();
   for (int t0 = 0; t0 < a.T; t0 += blockDim.x) {
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
     int jsel = -1;
     if (t < a.T) {
       for (int j = 0; j < a.top_k; ++j)
-        if (a.topk_idx[(size_t)t * a.top_k + j] == ge) jsel = j;
+        if (a.topk_idx[(size_t)t * stride + j] == ge) jsel = j;
     }
     const unsigned ballot = __ballot_sync(0xffffffffu, jsel >= 0);
     if (lane == 0) s_warp[warp] = __popc(ballot);
@@ -250,10 +251,9 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
     const int base = s_base;
     if (jsel >= 0) {
       const int r = base + warp_excl + __popc(ballot & ((1u << lane) - 1u));
-      const size_t o = (size_t)t * a.top_k + jsel;
       a.row_token[r] = t;
-      a.row_weight[r] = a.topk_w[o];
-      a.pair_row[o] = r;
+      a.row_weight[r] = a.topk_w[(size_t)t * stride + jsel];
+      a.pair_row[(size_t)t * a.top_k + jsel] = r;
     }
     __syncthreads();
     if (tid == 0) s_base = base + s_warp[nwarps - 1];

@@ -1,0 +1,181 @@
+"""Expert-parallel MoE layer over torch.distributed (NCCL on B200).
+
+The reference has no distributed code; its only hook is ``local_expert_offset``
+(``flashinfer_baseline.py:132-138``): one call computes the experts
+``[offset, offset + E_local)``.  Here rank ``r`` of ``W`` owns experts
+``[r*E/W, (r+1)*E/W)`` and ``T_r`` tokens; router weights, bias and the shared
+expert are replicated.  One layer forward on every rank:
+
+1. router GEMM + CUDA router over the rank's own tokens;
+2. dispatch plan: each token goes once to every rank holding any of its top-k
+   experts (group-limited routing bounds this at ``topk_group`` ranks when
+   groups align with ranks, e.g. EP8 of DeepSeek-V3), rows grouped by
+   destination in token order, quantised per 1x128 and packed with the ids and
+   weights of the experts on the destination;
+3. count exchange (``all_to_all_single`` of int32, then one host read of the
+   split sizes) and the dispatch ``all_to_all_single`` of packed rows -- the
+   shared expert runs on the rank's own tokens meanwhile;
+4. grouped GEMMs over the received rows, each row's result pre-reduced over its
+   local experts in fp32;
+5. ``all_to_all_single`` back and a deterministic gather-sum per token plus the
+   shared expert, cast to bf16.
+
+Every rank issues the same collectives in the same order.  The device work
+goes through a ``kernels`` object: :class:`CudaEpKernels` (the C ABI) by
+default; tests pass CPU stand-ins to exercise the exchange logic on gloo ranks.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+BLOCK = 128
+
+
+def row_bytes(H: int, top_k: int) -> int:
+    """Bytes of one packed dispatch row (``gemms_ep_row_bytes``)."""
+    raw = H + 4 * (H // BLOCK) + 8 * top_k
+    return (raw + 15) // 16 * 16
+
+
+class CudaEpKernels:
+    """Device side of expert parallelism through ``include/gemms_moe.h``."""
+
+    def __init__(self):
+        self.L = _lib.load()
+        self._ws = {}
+
+    @staticmethod
+    def _stream() -> int:
+        return torch.cuda.current_stream().cuda_stream
+
+    def _workspace(self, dev, nbytes: int, tag: str) -> torch.Tensor:
+        key = (dev.index, tag)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes + 256:
+            ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+            self._ws[key] = ws
+        off = (-ws.data_ptr()) % 256
+        return ws[off:off + nbytes]
+
+    def router_logits(self, x, router_w):
+        from .ops import router_logits
+        return router_logits(x, router_w)
+
+    def route(self, logits, bias, n_group, topk_group, top_k, rsf):
+        from .ops import route
+        idx, w, _ = route(logits, bias, n_group=n_group, topk_group=topk_group, top_k=top_k,
+                          routed_scaling_factor=rsf, counts=False)
+        return idx, w
+
+    def dispatch(self, idx, w, x, world: int, E_local: int):
+        T, H = x.shape
+        k = idx.shape[1]
+        dev = x.device
+        rb = row_bytes(H, k)
+        send_counts = torch.empty((world,), dtype=torch.int32, device=dev)
+        send_row_of = torch.empty((T, world), dtype=torch.int32, device=dev)
+        send_buf = torch.empty((max(T * min(world, k), 1), rb), dtype=torch.uint8, device=dev)
+        xq = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+        xq_scale = torch.empty((H // BLOCK, T), dtype=torch.float32, device=dev)
+        _lib.check(self.L.gemms_ep_dispatch(idx.data_ptr(), w.data_ptr(), x.data_ptr(), T, H, k, world, E_local,
+                                            send_counts.data_ptr(), send_row_of.data_ptr(), send_buf.data_ptr(),
+                                            xq.data_ptr(), xq_scale.data_ptr(), self._stream()),
+                   "gemms_ep_dispatch")
+        return send_counts, send_row_of, send_buf, xq, xq_scale
+
+    def expert_ffn(self, recv_buf, R: int, H: int, I: int, top_k: int, E_local: int, offset: int, planes: int,
+                   w13, w13_scale, w2, w2_scale):
+        dev = w13.device
+        out = torch.empty((max(R, 1), H), dtype=torch.float32, device=dev)
+        nbytes = self.L.gemms_ep_ffn_workspace_size(R, H, I, E_local, top_k, planes)
+        if nbytes == 0:
+            raise ValueError("unsupported expert-parallel FFN geometry")
+        ws = self._workspace(dev, nbytes, "ep_ffn")
+        _lib.check(self.L.gemms_ep_expert_ffn(recv_buf.data_ptr(), R, H, I, top_k, E_local, offset, planes,
+                                              w13.data_ptr(), w13_scale.data_ptr(), w2.data_ptr(),
+                                              w2_scale.data_ptr(), out.data_ptr(), ws.data_ptr(), nbytes,
+                                              self._stream()), "gemms_ep_expert_ffn")
+        return out[:R]
+
+    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes: int, acc):
+        """acc[T, H] (fp32) += shared expert of the token-major quantised rows."""
+        T, H = xq.shape
+        I = sw2.shape[1]
+        dev = xq.device
+        counts = torch.full((1,), T, dtype=torch.int32, device=dev)
+        dest = torch.arange(T, dtype=torch.int32, device=dev)
+        wts = torch.ones((T,), dtype=torch.float32, device=dev)
+        nbytes = self.L.gemms_expert_ffn_workspace_size(T, H, I, 1, planes)
+        ws = self._workspace(dev, nbytes, "shared_ffn")
+        _lib.check(self.L.gemms_expert_ffn(xq.data_ptr(), xq_scale.data_ptr(), T, counts.data_ptr(), dest.data_ptr(),
+                                           wts.data_ptr(), H, I, 1, planes, sw13.data_ptr(), sw13_scale.data_ptr(),
+                                           sw2.data_ptr(), sw2_scale.data_ptr(), acc.data_ptr(), ws.data_ptr(),
+                                           nbytes, self._stream()), "gemms_expert_ffn(shared)")
+        self._keep = (counts, dest, wts)  # alive until the stream has consumed them
+
+    def combine(self, acc, back, send_row_of, world: int):
+        T, H = acc.shape
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=acc.device)
+        _lib.check(self.L.gemms_ep_combine(acc.data_ptr(), back.data_ptr() if back.numel() else None,
+                                           send_row_of.data_ptr(), T, H, world, out.data_ptr(), self._stream()),
+                   "gemms_ep_combine")
+        return out
+
+
+_default_kernels = None
+
+
+def _cuda_kernels() -> CudaEpKernels:
+    global _default_kernels
+    if _default_kernels is None:
+        _default_kernels = CudaEpKernels()
+    return _default_kernels
+
+
+@torch.no_grad()
+def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13=None, shared_w13_scale=None,
+           shared_w2=None, shared_w2_scale=None, n_group=8, topk_group=4, top_k=8, routed_scaling_factor=2.5,
+           inter_planes=2, logits=None, group=None, kernels=None):
+    """Expert-parallel layer forward on this rank's tokens ``x`` [T_r, H].
+
+    ``w13``/``w2`` (and scales) hold this rank's ``E/W`` experts; the rank's
+    first global expert is ``rank * E/W``.
+    """
+    K = kernels if kernels is not None else _cuda_kernels()
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    E = router_w.shape[0]
+    E_local = w13.shape[0]
+    if E_local * world != E:
+        raise ValueError(f"each rank must hold E/world experts: E={E}, world={world}, local={E_local}")
+    T, H = x.shape
+    I = w13.shape[1] // 2
+    if logits is None:
+        logits = K.router_logits(x, router_w)
+    idx, wts = K.route(logits, router_bias, n_group, topk_group, top_k, routed_scaling_factor)
+    send_counts, send_row_of, send_buf, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local)
+
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    both = torch.stack([send_counts, recv_counts]).cpu()  # the one host synchronisation of the layer
+    sc, rc = [int(v) for v in both[0]], [int(v) for v in both[1]]
+    S, R = sum(sc), sum(rc)
+    rb = send_buf.shape[1]
+    recv_buf = torch.empty((R, rb), dtype=torch.uint8, device=send_buf.device)
+    work = dist.all_to_all_single(recv_buf, send_buf[:S].contiguous(), rc, sc, group=group, async_op=True)
+
+    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
+    if shared_w13 is not None:  # overlaps with the dispatch all-to-all
+        K.shared_ffn(xq, xq_scale, shared_w13, shared_w13_scale, shared_w2, shared_w2_scale, inter_planes, acc)
+    work.wait()
+
+    out_rows = K.expert_ffn(recv_buf, R, H, I, top_k, E_local, rank * E_local, inter_planes,
+                            w13, w13_scale, w2, w2_scale)
+    back = torch.empty((S, H), dtype=torch.float32, device=x.device)
+    dist.all_to_all_single(back, out_rows.contiguous(), sc, rc, group=group)
+    return K.combine(acc, back, send_row_of, world)

@@ -133,6 +133,36 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
                      const void* w13, const float* w13_scale, const void* w2, const float* w2_scale,
                      float* out_f32, void* workspace, size_t ws_bytes, gemms_stream_t stream);
 
+/* ---- expert parallel (rank r owns experts [r*E_local, (r+1)*E_local)) ----
+ * No counterpart in the reference, which has only the local_expert_offset
+ * slicing hook (flashinfer_baseline.py:132-138); the all-to-alls are NCCL
+ * calls made by the host (gemms_b200/ep.py).
+ *
+ * Packed dispatch row: e4m3 [H] | fp32 scales [H/128] | int32 expert ids
+ * [top_k] (-1 = not on the destination) | fp32 weights [top_k], padded to 16 B. */
+size_t gemms_ep_row_bytes(int32_t H, int32_t top_k);
+
+/* topk_idx/topk_w [T, top_k] (global ids) + x bf16 [T, H] ->
+ * send_counts [world] (zeroed here), send_row_of [T, world] (-1 = not sent),
+ * send_buf [<= T*min(world,top_k), row_bytes] grouped by destination in token
+ * order, and the token-major quantised rows xq [T, H] + xq_scale [H/128, T]. */
+int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* x_bf16, int32_t T, int32_t H,
+                      int32_t top_k, int32_t world, int32_t E_local, int32_t* send_counts, int32_t* send_row_of,
+                      void* send_buf, void* xq, float* xq_scale, gemms_stream_t stream);
+
+/* Received packed rows [R, row_bytes] -> out_rows fp32 [R, H] (overwritten):
+ * each row's results summed over its experts on this rank, times weights. */
+size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t H, int32_t I, int32_t E_local, int32_t top_k,
+                                   int32_t inter_planes);
+int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, int32_t top_k, int32_t E_local,
+                        int32_t local_expert_offset, int32_t inter_planes, const void* w13, const float* w13_scale,
+                        const void* w2, const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
+                        gemms_stream_t stream);
+
+/* out bf16 [T, H] = acc fp32 [T, H] + sum over d of back_rows[send_row_of[t, d]]. */
+int gemms_ep_combine(const float* acc, const float* back_rows, const int32_t* send_row_of, int32_t T, int32_t H,
+                     int32_t world, void* out_bf16, gemms_stream_t stream);
+
 /* Reads and clears the device error word kept in a gemms_moe_fwd workspace.
  * Synchronises the stream.  *flags receives the raw bit set (0 = clean). */
 int gemms_moe_check(void* workspace, gemms_stream_t stream, int32_t* flags);

@@ -1,0 +1,91 @@
+"""CPU stand-ins for the device side of expert parallelism (test-only).
+
+They follow the contracts of ``include/gemms_moe.h`` (packed row layout,
+destination grouping in token order, fp32 pre-reduced rows, deterministic
+combine) with the oracle's fp32 arithmetic, so that ``gemms_b200.ep.moe_ep``'s
+host logic -- count exchange, split sizes, the two all-to-alls and the
+combine mapping -- runs on gloo ranks without a GPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from gemms_b200 import ep as EP
+from oracle import reference_moe as R
+
+BLOCK = 128
+
+
+class CpuEpKernels:
+    def __init__(self, n_group, topk_group, top_k):
+        self.ng, self.tg, self.k = n_group, topk_group, top_k
+
+    def router_logits(self, x, router_w):
+        return R.router_logits(x, router_w)
+
+    def route(self, logits, bias, n_group, topk_group, top_k, rsf):
+        idx, dense, _, _ = R.route(logits, bias, n_group, topk_group, top_k, rsf)
+        return idx.to(torch.int32), torch.gather(dense, 1, idx)
+
+    def dispatch(self, idx, w, x, world, E_local):
+        T, H = x.shape
+        k = idx.shape[1]
+        rb = EP.row_bytes(H, k)
+        KB = H // BLOCK
+        xq, xq_scale = R.quantize_1x128(x)
+        dests = (idx.long() // E_local)
+        send_row_of = torch.full((T, world), -1, dtype=torch.int32)
+        rows = []
+        counts = torch.zeros(world, dtype=torch.int32)
+        for d in range(world):
+            for t in range(T):
+                if bool((dests[t] == d).any()):
+                    send_row_of[t, d] = len(rows)
+                    rows.append((t, d))
+                    counts[d] += 1
+        buf = torch.zeros((max(len(rows), 1), rb), dtype=torch.uint8)
+        for r, (t, d) in enumerate(rows):
+            buf[r, :H] = xq[t].view(torch.uint8)
+            buf[r, H:H + 4 * KB] = xq_scale[:, t].contiguous().view(torch.uint8)
+            here = dests[t] == d
+            ids = torch.where(here, idx[t].long(), torch.full_like(idx[t].long(), -1)).to(torch.int32)
+            ws = torch.where(here, w[t], torch.zeros_like(w[t])).to(torch.float32)
+            buf[r, H + 4 * KB:H + 4 * KB + 4 * k] = ids.view(torch.uint8)
+            buf[r, H + 4 * KB + 4 * k:H + 4 * KB + 8 * k] = ws.view(torch.uint8)
+        return counts, send_row_of, buf, xq, xq_scale
+
+    def expert_ffn(self, recv_buf, Rn, H, I, top_k, E_local, offset, planes, w13, w13_scale, w2, w2_scale):
+        KB = H // BLOCK
+        out = torch.zeros((Rn, H), dtype=torch.float32)
+        if Rn == 0:
+            return out
+        xq = recv_buf[:Rn, :H].contiguous().view(torch.float8_e4m3fn)
+        sc = recv_buf[:Rn, H:H + 4 * KB].contiguous().view(torch.float32)          # [R, KB]
+        ids = recv_buf[:Rn, H + 4 * KB:H + 4 * KB + 4 * top_k].contiguous().view(torch.int32)
+        ws = recv_buf[:Rn, H + 4 * KB + 4 * top_k:H + 4 * KB + 8 * top_k].contiguous().view(torch.float32)
+        A = R.dequant_hidden(xq, sc.t().contiguous())
+        for le in range(E_local):
+            sel = (ids == offset + le)
+            rows = sel.any(1).nonzero().squeeze(1)
+            if rows.numel() == 0:
+                continue
+            W13 = R.dequant_weight(w13[le], w13_scale[le])
+            W2 = R.dequant_weight(w2[le], w2_scale[le])
+            G1 = A[rows] @ W13.t()
+            C = (G1[:, I:] / (1.0 + torch.exp(-G1[:, I:]))) * G1[:, :I]
+            O = C @ W2.t()
+            wt = (ws[rows] * sel[rows]).sum(1)
+            out.index_add_(0, rows, O * wt.unsqueeze(1))
+        return out
+
+    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes, acc):
+        acc += R.shared_expert(R.dequant_hidden(xq, xq_scale), sw13, sw13_scale, sw2, sw2_scale)
+
+    def combine(self, acc, back, send_row_of, world):
+        out = acc.clone()
+        for t in range(acc.shape[0]):
+            for d in range(world):
+                r = int(send_row_of[t, d])
+                if r >= 0:
+                    out[t] += back[r]
+        return out.to(torch.bfloat16)

@@ -1,0 +1,110 @@
+"""CPU, world_size 2 (gloo): expert-parallel host logic of gemms_b200.ep.
+
+The device side is replaced by CPU stand-ins (tests/ep_fakes.py) that follow
+the C ABI's contracts with the oracle's arithmetic; the exchange itself (count
+all-to-all, split sizes, dispatch and combine all-to-alls, combine mapping) is
+the product code.  The 2-rank result must equal the single-process oracle over
+all tokens.  A second test makes one rank leave before the first collective:
+the remaining rank must raise within its process-group timeout, not hang.
+"""
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gemms_b200 import ep as EP
+from gemms_b200 import workloads as W
+from oracle import reference_moe as R
+
+SHAPE = W.CONFIGS["c0"].replace(T=48, shared=True)  # E=32, 4 groups / top-2 groups / top-4
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _inputs():
+    return W.make_inputs(SHAPE, seed=4)
+
+
+def _ep_worker(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from tests.ep_fakes import CpuEpKernels
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    d = _inputs()
+    T = SHAPE.T // world
+    El = SHAPE.E // world
+    sl = slice(rank * T, (rank + 1) * T)
+    el = slice(rank * El, (rank + 1) * El)
+    K = CpuEpKernels(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
+    out = EP.moe_ep(d["x"][sl], d["router_w"], d["router_bias"], d["w13"][el], d["w13_scale"][el], d["w2"][el],
+                    d["w2_scale"][el], shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"],
+                    shared_w2=d["shared_w2"], shared_w2_scale=d["shared_w2_scale"], n_group=SHAPE.n_group,
+                    topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, routed_scaling_factor=SHAPE.rsf,
+                    group=dist.group.WORLD, kernels=K)
+    torch.save(out, os.path.join(outdir, f"out{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_two_ranks_matches_single_process_oracle():
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_ep_worker, args=(world, _free_port(), tmp), nprocs=world, join=True)
+        got = torch.cat([torch.load(os.path.join(tmp, f"out{r}.pt")) for r in range(world)])
+    d = _inputs()
+    ref = R.moe_layer(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+                      d["shared_w13"], d["shared_w13_scale"], d["shared_w2"], d["shared_w2_scale"],
+                      n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, rsf=SHAPE.rsf)
+    m = R.compare(got, ref)
+    # same fp32 arithmetic, different summation order across ranks
+    assert m["mae_rms"] < 1e-4 and m["max_rel"] < 1e-2, m
+
+
+def _leaver_worker(rank, world, port, outdir):
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from tests.ep_fakes import CpuEpKernels
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        return  # leaves between steps: never joins the layer's collectives
+    d = _inputs()
+    T, El = SHAPE.T // world, SHAPE.E // world
+    K = CpuEpKernels(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
+    t0 = time.time()
+    status = "no-error"
+    try:
+        EP.moe_ep(d["x"][:T], d["router_w"], d["router_bias"], d["w13"][:El], d["w13_scale"][:El], d["w2"][:El],
+                  d["w2_scale"][:El], n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k,
+                  routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K)
+    except RuntimeError as e:  # gloo: timeout or connection closed by the departed peer
+        status = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
+    with open(os.path.join(outdir, "status.txt"), "w") as f:
+        f.write(status)
+
+
+def test_ep_rank_that_never_joins_is_detected():
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_leaver_worker, args=(world, _free_port(), tmp), nprocs=world, join=True)
+        status = open(os.path.join(tmp, "status.txt")).read()
+    assert status.startswith("error after"), status
+    secs = float(status.split()[2].rstrip("s:"))
+    assert secs < 30, status
