@@ -11,8 +11,10 @@ combine + shared expert -> bf16) over one batch of synthetic tokens.
   top-4 groups / top-8, scaling 2.5, + 1 shared expert.  Inputs are resident in
   HBM; every step streams 11.3 GB of expert weights, far larger than the 126 MB
   L2, so no flush is needed between steps.
-* N>1 (torchrun): BASELINE config c3 -- expert-parallel over N ranks, T=32768
-  tokens in total (32768/N per rank), E/N experts per rank, NCCL all-to-all.
+* N>1 (torchrun): expert parallel over N ranks with the per-rank work of c1
+  held fixed -- 4096 tokens and E/N experts per rank, T = 4096*N in total, NCCL
+  all-to-all -- so value(N) / (N * value(1)) is a weak-scaling efficiency.  At
+  N=8 this is exactly BASELINE config c3 (T=32768, 32 experts per GPU).
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
 implementation of the path (the oracle restatement in ``oracle/``, bit-identical
@@ -287,7 +289,7 @@ def gpu_arm(a):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
-    cfg = a.config or ("c1" if world == 1 else "c3")
+    cfg = a.config or ("c1" if world == 1 else f"c3:T={4096 * world}")
     base = parse_config(cfg)
     T_rank = base.T // world if world > 1 else base.T
     sh = base.replace(T=T_rank)
