@@ -162,13 +162,15 @@ def algorithmic_bytes(sh, counts, planes: int, world: int = 1):
     return {"gemm1": g1, "gemm2": g2, "experts_hit": hit, "rows": rows}
 
 
-def _traffic(kernel: str):
-    """DRAM bytes per launch from the committed ncu capture summary, if any."""
+def _traffic(kernel: str, algorithmic_bytes: float):
+    """DRAM bytes per launch from the committed ncu capture (profiles/dram_traffic.json):
+    the measured traffic/algorithmic ratio of that capture times this launch's
+    algorithmic bytes.  None if there is no capture for the kernel."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d.get(kernel)
+        return float(d[kernel]["ratio"]) * algorithmic_bytes
     except Exception:
         return None
 
@@ -427,14 +429,14 @@ def gpu_arm(a):
         ab = algorithmic_bytes(sh, counts_cpu, planes)
         g1_gbs = ab["gemm1"] / (g1_ms / 1e3) / 1e9
         g2_gbs = ab["gemm2"] / (g2_ms / 1e3) / 1e9
-        tr = _traffic("gemm1")
+        tr = _traffic("gemm1", ab["gemm1"])
         line["roofline"] = {"bound": "hbm", "kernel": "grouped_gemm_kernel<0,1,2> (GEMM1 + SwiGLU + requant)",
                             "achieved": g1_gbs, "peak": hbm, "unit": "GB/s", "frac": g1_gbs / hbm,
                             "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else
                             "fallback 6650 GB/s", "traffic": tr,
                             "algorithmic_bytes": ab["gemm1"], "launch_ms": g1_ms}
         line["kernels"] = {"gemm1": {"ms": g1_ms, "GB/s": g1_gbs, "bytes": ab["gemm1"]},
-                           "gemm2": {"ms": g2_ms, "GB/s": g2_gbs, "bytes": ab["gemm2"], "traffic": _traffic("gemm2")},
+                           "gemm2": {"ms": g2_ms, "GB/s": g2_gbs, "bytes": ab["gemm2"], "traffic": _traffic("gemm2", ab["gemm2"])},
                            "layer": {"ms": ms, "hbm_frac_of_layer_floor":
                                      (ab["gemm1"] + ab["gemm2"]) / 1e9 / hbm / (ms / 1e3)},
                            "experts_hit": ab["experts_hit"], "rows": ab["rows"]}
