@@ -58,12 +58,16 @@ constexpr uint32_t kTmemCols = 512;     // 2 partial accumulators x 256 columns
 constexpr int kTileA = BM * BK;         // 16 KB
 constexpr int kTileB = BN * BK;         // 32 KB
 
+constexpr int kEpiWarpsCfg = 8;
+
 template <int PLANES>
 struct Cfg {
   static constexpr int kStageBytes = PLANES * kTileA + kTileB;
   static constexpr int kStages = PLANES == 1 ? 4 : (PLANES == 2 ? 3 : 2);
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kSmemBytes = kRingBytes + 4096 + 1024;  // + barriers/exchange + alignment slack
+  // GEMM2 (PLANES > 1) stages its combine writes: 8 warps x 32 rows x 20 floats.
+  static constexpr int kStageOutBytes = PLANES > 1 ? kEpiWarpsCfg * 32 * 20 * 4 : 0;
+  static constexpr int kSmemBytes = kRingBytes + 4096 + kStageOutBytes + 1024;  // + barriers/exchange + slack
 };
 
 struct GemmParams {
@@ -387,7 +391,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
           const float up = acc[64 + j];
-          const float cval = __fdiv_rn(up, 1.0f + expf(-up)) * acc[j];
+          // silu(up) = up * 1/(1 + e^-up); a saturated e^-up gives 1/inf = 0.
+          const float cval = up * __frcp_rn(1.0f + __expf(-up)) * acc[j];
           acc[j] = cval;
           amax = fmaxf(amax, fabsf(cval));
         }
@@ -396,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(1, kEpiWarps * 32);
         amax = fmaxf(amax, ax[(1 - h) * 128 + r]);
         const float scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+        const float inv = amax > 0.f ? __fdiv_rn(kFp8Max, amax) : 1.0f;
         if (valid) {
           const size_t row_bytes = (size_t)OUT_PLANES * p.I;
           uint8_t* dst = p.inter + (size_t)(row0 + r) * row_bytes + (size_t)nt * kBlock + 64 * h;
@@ -404,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t w[OUT_PLANES][4];
 #pragma unroll
             for (int j = 0; j < 16; j += 2) {
-              float x0 = __fdiv_rn(acc[j0 + j], scale), x1 = __fdiv_rn(acc[j0 + j + 1], scale);
+              float x0 = acc[j0 + j] * inv, x1 = acc[j0 + j + 1] * inv;
 #pragma unroll
               for (int pl = 0; pl < OUT_PLANES; ++pl) {
                 const uint16_t b2 = f2_to_e4m3x2(x0, x1);
@@ -426,14 +432,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (h == 0) p.inter_scale[(size_t)nt * p.inter_scale_ld + row0 + r] = scale;
         }
       } else {
-        if (valid) {
-          const int dst = p.row_dest[row0 + r];
-          const float wgt = p.row_weight[row0 + r];
-          float* o = p.out + (size_t)dst * p.H + (size_t)nt * BN + 128 * h;
+        // Weighted rows are added into their tokens' fp32 output rows.  Lane =
+        // row in TMEM, so a direct float4 atomic per lane would touch 32 rows
+        // per instruction; instead each 32-row x 16-column chunk goes through
+        // shared memory and comes back with 4 lanes per row, so every vector
+        // RED covers 64 contiguous bytes of 8 rows.
+        float* stage = reinterpret_cast<float*>(smem + C::kRingBytes + 4096) + ew * (32 * 20);
+        const int dst_me = valid ? p.row_dest[row0 + r] : -1;
+        const float wgt = valid ? p.row_weight[row0 + r] : 0.f;
+        int dst_i[4];
 #pragma unroll
-          for (int c = 0; c < 128; c += 4)
-            atomicAdd(reinterpret_cast<float4*>(o + c),
-                      make_float4(wgt * acc[c], wgt * acc[c + 1], wgt * acc[c + 2], wgt * acc[c + 3]));
+        for (int i = 0; i < 4; ++i) dst_i[i] = __shfl_sync(0xffffffffu, dst_me, 8 * i + (lane >> 2));
+        float* obase = p.out + (size_t)nt * BN + 128 * h + 4 * (lane & 3);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<float4*>(stage + lane * 20 + 4 * k) =
+                make_float4(wgt * acc[16 * ch + 4 * k], wgt * acc[16 * ch + 4 * k + 1], wgt * acc[16 * ch + 4 * k + 2],
+                            wgt * acc[16 * ch + 4 * k + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int row = 8 * i + (lane >> 2);
+            if (dst_i[i] >= 0) {
+              const float4 v = *reinterpret_cast<const float4*>(stage + row * 20 + 4 * (lane & 3));
+              atomicAdd(reinterpret_cast<float4*>(obase + (size_t)dst_i[i] * p.H + 16 * ch), v);
+            }
+          }
+          __syncwarp();
         }
       }
     }
