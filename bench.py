@@ -299,6 +299,7 @@ def gpu_arm(a):
 
     # inputs: this rank's tokens; this rank's E/world experts (EP) or all E
     n_local = sh.E // world
+    zipf_hist = None
     d = W.make_inputs(sh, seed=rank, device=dev, experts=n_local)
     # every rank must hold the same router weights/bias and shared expert
     g = torch.Generator(device=dev).manual_seed(12345)
@@ -309,6 +310,15 @@ def gpu_arm(a):
         d["shared_w13_scale"] = torch.rand((2 * sh.I // 128, sh.H // 128), generator=g, device=dev) * 2e-3 + 1e-3
         d["shared_w2"] = torch.randn((sh.H, sh.I), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
         d["shared_w2_scale"] = torch.rand((sh.H // 128, sh.I // 128), generator=g, device=dev) * 2e-3 + 1e-3
+    if cfg.startswith("c4"):
+        # BASELINE c4: router bias calibrated so expert popularity follows
+        # Zipf(1.2) over a seeded permutation, hottest experts on ranks 0-1.
+        route_fn = lambda lg, b: gemms_b200.route(lg, b, n_group=sh.n_group, topk_group=sh.topk_group,
+                                                  top_k=sh.top_k, routed_scaling_factor=sh.rsf, counts=False)[0]
+        bias, frac = W.zipf_bias(sh, route_fn, router_w=d["router_w"], s=1.2, seed=0, hot_ranks=2, world=8,
+                                 device=dev)
+        d["router_bias"] = bias
+        zipf_hist = frac.cpu()
     shared_kw = {k: d[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale") if k in d}
     kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
               inter_planes=planes, ep_group=group, **shared_kw)
@@ -425,6 +435,10 @@ def gpu_arm(a):
             "tflops": flops / (ms / 1e3) / 1e12,
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
             "e2e": e2e, "clocks": clocks}
+    if zipf_hist is not None:
+        per_rank = zipf_hist.reshape(8, -1).sum(1)
+        line["config"]["zipf"] = {"s": 1.2, "top_expert_share": float(zipf_hist.max()),
+                                  "rank_share_of_routed_pairs": [round(float(v), 4) for v in per_rank]}
     if group is None:
         ab = algorithmic_bytes(sh, counts_cpu, planes)
         g1_gbs = ab["gemm1"] / (g1_ms / 1e3) / 1e9

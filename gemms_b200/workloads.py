@@ -132,8 +132,9 @@ def make_inputs(shape: MoeShape, seed: int = 0, device="cpu", experts: int | Non
     return d
 
 
-def zipf_bias(shape: MoeShape, route_fn, s: float = 1.2, seed: int = 0, hot_ranks: int = 2, world: int = 8,
-              iters: int = 60, probe_tokens: int = 4096, device="cpu") -> tuple[torch.Tensor, torch.Tensor]:
+def zipf_bias(shape: MoeShape, route_fn, router_w: torch.Tensor | None = None, s: float = 1.2, seed: int = 0,
+              hot_ranks: int = 2, world: int = 8, iters: int = 60, probe_tokens: int = 4096,
+              device="cpu") -> tuple[torch.Tensor, torch.Tensor]:
     """Calibrate a router bias so expert popularity follows Zipf(s) (config c4).
 
     The popularity ranking is a seeded permutation whose hottest experts sit on
@@ -142,7 +143,8 @@ def zipf_bias(shape: MoeShape, route_fn, s: float = 1.2, seed: int = 0, hot_rank
     damped fixed-point iteration on a probe batch until the routed histogram
     tracks the Zipf target; returns (bias, achieved_histogram_fraction).
     ``route_fn(logits, bias) -> topk_idx [T, top_k]`` is the router to calibrate
-    against (the CUDA router on a GPU box).
+    against (the CUDA router on a GPU box); ``router_w`` the router weights the
+    bias will be used with (default: this module's seeded draw).
     """
     E = shape.E
     g = torch.Generator(device="cpu").manual_seed(seed + 7)
@@ -157,7 +159,8 @@ def zipf_bias(shape: MoeShape, route_fn, s: float = 1.2, seed: int = 0, hot_rank
     target = torch.empty(E, dtype=torch.float64)
     target[order] = target_sorted
     probe = make_inputs(shape.replace(T=probe_tokens), seed=seed + 11, device=device, with_weights=False)
-    logits = probe["x"].float() @ probe["router_w"].t()
+    rw = probe["router_w"] if router_w is None else router_w.to(device)
+    logits = probe["x"].float() @ rw.float().t()
     bias = torch.zeros(E, dtype=torch.float32, device=device)
     target = target.to(device)
     frac = None
