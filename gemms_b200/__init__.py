@@ -7,11 +7,13 @@ Public operators (CUDA tensors only, no CPU fallback):
 * :func:`moe` -- the full layer ``moe(x, router_w, router_bias, w13, w13_scale,
   w2, w2_scale, ...)``, optionally expert-parallel over a process group.
 * :func:`route` -- the group-limited sigmoid top-k router alone.
+* :class:`MoePipeline` -- host-to-host serving loop with PCIe copies overlapped.
 """
 from .ops import ShapeError, check_device_errors, moe, route, router_logits, run  # noqa: F401
 from ._lib import GemmsError, lib_path, load as load_library  # noqa: F401
 from . import workloads  # noqa: F401
+from .pipeline import MoePipeline  # noqa: F401
 
 __all__ = ["run", "moe", "route", "router_logits", "ShapeError", "GemmsError", "check_device_errors",
-           "load_library", "lib_path", "workloads"]
+           "load_library", "lib_path", "workloads", "MoePipeline"]
 __version__ = "0.1.0"
