@@ -253,12 +253,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         for (int kb = 0; kb < p.kb_count; ++kb, ++it, ++acc_it) {
           const int buf = acc_it & 1;
-          if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          // The smem stage is normally ready long before the TMEM buffer is
+          // released, so its (cheap, satisfied) wait goes first and the
+          // buffer wait is the last step before the MMAs.
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, p.err, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
-          const int s = it % S;
-          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
@@ -391,8 +394,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
           const float up = acc[64 + j];
-          // silu(up) = up * 1/(1 + e^-up); a saturated e^-up gives 1/inf = 0.
-          const float cval = up * __frcp_rn(1.0f + __expf(-up)) * acc[j];
+          // silu(up) = up * 1/(1 + e^-up) with the hardware reciprocal (rel.
+          // error ~2^-23; C is requantised to e4m3 planes right after, and the
+          // IEEE-rounded reciprocal cost ~8k cycles per tile here).  A
+          // saturated e^-up gives 1/inf = 0.
+          const float cval = up * rcp_approx(1.0f + __expf(-up)) * acc[j];
           acc[j] = cval;
           amax = fmaxf(amax, fabsf(cval));
         }

@@ -188,6 +188,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Hardware reciprocal approximation (MUFU, flush-to-zero); 1/inf = 0.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // (a0, a1) += f * (v0, v1) as one packed fp32x2 FMA (sm_100 f32x2 pipe).
 __device__ __forceinline__ void ffma2(float& a0, float& a1, float f, float v0, float v1) {
   asm("{\n\t.reg .b64 acc, fv, vv;\n\t"
