@@ -6,13 +6,16 @@
 // * G1[:,:I]; O = C W2_e^T; out += w * O), and the reference's attempt at it,
 // persistent_gemm_kernel in persistent_kernel2.cu:388-890.
 //
-// Design (one persistent CTA per SM, 320 threads, warp-specialised):
+// Design (one persistent CTA per SM, 384 threads, warp-specialised; the
+// control warpgroup 0-3 runs on 40-56 registers, the epilogue warpgroups on
+// 224-232 via setmaxnreg):
 //   warp 0      TMA producer: A tile(s) [128 rows x 128 B] per plane and two
-//               128-row weight boxes per stage into a 3-4 deep smem ring.
+//               128-row weight boxes per stage into a 2-4 deep smem ring.
 //   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
 //               (M=128, N=256, K=32 e4m3) from one thread; each 128-wide K
 //               block goes to one of two TMEM partial accumulators.
-//   warps 2-9   "promotion" epilogue: for every K block read the fp32 partial
+//   warps 2-3   idle (setmaxnreg works per warpgroup).
+//   warps 4-11  "promotion" epilogue: for every K block read the fp32 partial
 //               from TMEM, multiply by a_scale[row,kb] * w_scale[nblk,kb] and
 //               accumulate in registers (the block scales are arbitrary fp32,
 //               so the MX block-scaled MMA kinds cannot absorb them).  Then:
