@@ -380,6 +380,25 @@ def gpu_arm(a):
         ms_total = float(tt.item())
     ms = ms_total / a.steps
 
+    ep_timeline = None
+    if group is not None:
+        # per-phase device time of the expert-parallel step (rank 0's stream),
+        # measured on extra steps after the timed region
+        from gemms_b200 import ep as ep_mod
+        marks = []
+        for _ in range(5):
+            tl = []
+            ep_mod.moe_ep(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                          d["w2_scale"], group=group, timeline=tl,
+                          **{k: v for k, v in kw.items() if k != "ep_group"})
+            marks.append(tl)
+        barrier()
+        recv_rows = [v for n, v in marks[0] if n == "recv_rows"][0]
+        marks = [[(n, e) for n, e in tl if n != "recv_rows"] for tl in marks]
+        names = [n for n, _ in marks[0]]
+        ep_timeline = {names[j]: round(statistics.median(tl[j - 1][1].elapsed_time(tl[j][1]) for tl in marks), 4)
+                       for j in range(1, len(names))}
+        ep_timeline["recv_rows"] = recv_rows
     g1_ms = statistics.mean(evs[i][0].elapsed_time(evs[i][1]) for i in range(nev)) if nev else None
     g2_ms = statistics.mean(evs[i][1].elapsed_time(evs[i][2]) for i in range(nev)) if nev else None
     if group is None:
@@ -440,6 +459,21 @@ def gpu_arm(a):
         per_rank = zipf_hist.reshape(8, -1).sum(1)
         line["config"]["zipf"] = {"s": 1.2, "top_expert_share": float(zipf_hist.max()),
                                   "rank_share_of_routed_pairs": [round(float(v), 4) for v in per_rank]}
+    if group is not None:
+        # Dominant phase at N>1: the grouped GEMMs over the received rows
+        # (GEMM1 + GEMM2 of the rank's E/N experts, all of them hit at c3).
+        R = ep_timeline["recv_rows"]
+        ffn_bytes = (n_local * 3 * sh.I * sh.H + R * sh.H + 2 * R * planes * 2 * sh.I + 4 * R * sh.H
+                     + (3 * sh.I * sh.H + sh.T * sh.H if sh.shared else 0))
+        ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) if sh.shared else 0.0)
+        ach = ffn_bytes / (ffn_ms / 1e3) / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": "grouped GEMM1+GEMM2 over received rows + shared expert "
+                                                      "(rank 0, expert_ffn + shared_ffn phases)",
+                            "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                            "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else
+                            "fallback 6650 GB/s", "traffic": None, "algorithmic_bytes": ffn_bytes,
+                            "launch_ms": ffn_ms}
+        line["ep_timeline_ms"] = ep_timeline
     if group is None:
         ab = algorithmic_bytes(sh, counts_cpu, planes)
         g1_gbs = ab["gemm1"] / (g1_ms / 1e3) / 1e9

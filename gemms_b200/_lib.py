@@ -33,6 +33,8 @@ EXPORTS = (
     "gemms_ep_dispatch",
     "gemms_ep_ffn_workspace_size",
     "gemms_ep_expert_ffn",
+    "gemms_ep_back_row_bytes",
+    "gemms_ep_pack_back",
     "gemms_ep_combine",
 )
 
@@ -119,6 +121,10 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                           c_void_p]
         L.gemms_ep_expert_ffn.restype = c_int32
+        L.gemms_ep_back_row_bytes.argtypes = [c_int32]
+        L.gemms_ep_back_row_bytes.restype = c_size_t
+        L.gemms_ep_pack_back.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p]
+        L.gemms_ep_pack_back.restype = c_int32
         L.gemms_ep_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
         L.gemms_ep_combine.restype = c_int32
         _lib = L

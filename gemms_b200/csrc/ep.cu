@@ -17,6 +17,11 @@
 //               histogram -> plan -> assign -> permute -> GEMM1 -> GEMM2; each
 //               received row's result is pre-reduced over its local experts in
 //               fp32.
+//   pack back : each pre-reduced fp32 row is sent back as fp16 values divided
+//               by a per-row power of two 2^e (max|row| / 2^e < 2^15), so the
+//               scaling is exact and the only new rounding is fp16's (2^-11
+//               relative, below the output's bf16 rounding); halves the bytes
+//               of the combine all-to-all.
 //   combine   : out[t] = bf16(acc[t] + sum over t's destinations of the rows
 //               sent back), gathered deterministically.
 //
@@ -25,7 +30,11 @@
 //   [H, H + 4*H/128)          fp32 1x128 scales
 //   [.., + 4*top_k)           int32 global expert ids on the destination, -1 padded
 //   [.., + 4*top_k)           fp32 routing weights
+// Packed combine row (back_row_bytes = align16(2*H + 4)):
+//   [0, 2H)                   fp16 values / 2^e
+//   [2H, 2H + 4)              fp32 2^e
 #include "common.cuh"
+#include <cuda_fp16.h>
 
 #include <algorithm>
 
@@ -37,6 +46,8 @@ constexpr int kMaxWorld = 32;
 __host__ __device__ inline size_t ep_row_bytes(int H, int top_k) {
   return align_up((size_t)H + 4 * (size_t)(H / kBlock) + 8 * (size_t)top_k, 16);
 }
+
+__host__ __device__ inline size_t ep_back_row_bytes(int H) { return align_up(2 * (size_t)H + 4, 16); }
 
 __device__ __forceinline__ unsigned dest_mask(const int32_t* idx, int top_k, int E_local) {
   unsigned m = 0;
@@ -183,25 +194,65 @@ __global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_byte
 }
 
 // Block per token: out[t] = bf16(acc[t] + sum of the token's returned rows).
+// Block per row: amax, then the row's values divided by 2^e as fp16.
+__global__ void __launch_bounds__(256) ep_pack_back_kernel(const float* __restrict__ rows, int H,
+                                                           uint8_t* __restrict__ packed, size_t rbb) {
+  __shared__ float s_warp[8];
+  const size_t r = blockIdx.x;
+  const float4* src = reinterpret_cast<const float4*>(rows + r * H);
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+    const float4 v = src[c];
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = s_warp[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, s_warp[w]);
+  // amax = m * 2^x with m in [0.5, 1): amax < 2^x, so e = x - 15 keeps every
+  // |value| / 2^e below 2^15 (fp16 max 65504).  Zero / non-finite rows: e = 0.
+  int x = 0;
+  if (amax > 0.f && isfinite(amax)) frexpf(amax, &x), x -= 15;
+  uint8_t* dst = packed + r * rbb;
+  for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+    const float4 v = src[c];
+    const __half2 lo = __floats2half2_rn(ldexpf(v.x, -x), ldexpf(v.y, -x));
+    const __half2 hi = __floats2half2_rn(ldexpf(v.z, -x), ldexpf(v.w, -x));
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst + 8 * (size_t)c) = o;
+  }
+  if (threadIdx.x == 0) *reinterpret_cast<float*>(dst + 2 * (size_t)H) = ldexpf(1.0f, x);
+}
+
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc,
-                                                         const float* __restrict__ back,
+                                                         const uint8_t* __restrict__ back, size_t rbb,
                                                          const int32_t* __restrict__ send_row_of, int T, int H,
                                                          int world, __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
   int rows[kMaxWorld];
+  float scale[kMaxWorld];
   int nd = 0;
   for (int d = 0; d < world; ++d) {
     const int r = send_row_of[(size_t)t * world + d];
-    if (r >= 0) rows[nd++] = r;
+    if (r >= 0) {
+      rows[nd] = r;
+      scale[nd] = *reinterpret_cast<const float*>(back + (size_t)r * rbb + 2 * (size_t)H);
+      ++nd;
+    }
   }
   for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
     float4 s = *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
     for (int i = 0; i < nd; ++i) {
-      const float4 b = *reinterpret_cast<const float4*>(back + (size_t)rows[i] * H + c);
-      s.x += b.x;
-      s.y += b.y;
-      s.z += b.z;
-      s.w += b.w;
+      const uint2 b = *reinterpret_cast<const uint2*>(back + (size_t)rows[i] * rbb + 2 * (size_t)c);
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
+      s.x = fmaf(lo.x, scale[i], s.x);
+      s.y = fmaf(lo.y, scale[i], s.y);
+      s.z = fmaf(hi.x, scale[i], s.z);
+      s.w = fmaf(hi.y, scale[i], s.w);
     }
     __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
     uint2 o;
@@ -410,14 +461,28 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   return launch_gemm2(g2, st);
 }
 
-int gemms_ep_combine(const float* acc, const float* back_rows, const int32_t* send_row_of, int32_t T, int32_t H,
+size_t gemms_ep_back_row_bytes(int32_t H) { return H > 0 ? ep_back_row_bytes(H) : 0; }
+
+int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, gemms_stream_t stream_) {
+  if (R < 0 || H <= 0 || H % 4) return GEMMS_ERR_SHAPE;
+  if (R == 0) return GEMMS_OK;
+  if (!rows || !packed) return GEMMS_ERR_ARG;
+  if (!aligned16(rows) || !aligned16(packed)) return GEMMS_ERR_ALIGN;
+  ep_pack_back_kernel<<<R, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      rows, H, static_cast<uint8_t*>(packed), ep_back_row_bytes(H));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* send_row_of, int32_t T, int32_t H,
                      int32_t world, void* out_bf16, gemms_stream_t stream_) {
   if (T < 0 || H <= 0 || H % 4 || world < 1 || world > kMaxWorld) return GEMMS_ERR_SHAPE;
-  if (!acc || !send_row_of || !out_bf16) return GEMMS_ERR_ARG;  // back_rows may be NULL when nothing was sent
-  if (!aligned16(acc) || !aligned16(out_bf16) || (back_rows && !aligned16(back_rows))) return GEMMS_ERR_ALIGN;
+  if (!acc || !send_row_of || !out_bf16) return GEMMS_ERR_ARG;  // back_packed may be NULL when nothing was sent
+  if (!aligned16(acc) || !aligned16(out_bf16) || (back_packed && !aligned16(back_packed))) return GEMMS_ERR_ALIGN;
   if (T == 0) return GEMMS_OK;
   ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      acc, back_rows, send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+      acc, static_cast<const uint8_t*>(back_packed), ep_back_row_bytes(H), send_row_of, T, H, world,
+      static_cast<__nv_bfloat16*>(out_bf16));
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

@@ -17,8 +17,9 @@ expert are replicated.  One layer forward on every rank:
    shared expert runs on the rank's own tokens meanwhile;
 4. grouped GEMMs over the received rows, each row's result pre-reduced over its
    local experts in fp32;
-5. ``all_to_all_single`` back and a deterministic gather-sum per token plus the
-   shared expert, cast to bf16.
+5. the rows go back as fp16 with a per-row power-of-two scale (exact
+   scaling, half the bytes of fp32), ``all_to_all_single``, and a
+   deterministic gather-sum per token plus the shared expert, cast to bf16.
 
 Every rank issues the same collectives in the same order.  The device work
 goes through a ``kernels`` object: :class:`CudaEpKernels` (the C ABI) by
@@ -40,6 +41,11 @@ def row_bytes(H: int, top_k: int) -> int:
     """Bytes of one packed dispatch row (``gemms_ep_row_bytes``)."""
     raw = H + 4 * (H // BLOCK) + 8 * top_k
     return (raw + 15) // 16 * 16
+
+
+def back_row_bytes(H: int) -> int:
+    """Bytes of one packed combine row (``gemms_ep_back_row_bytes``): fp16 [H] + fp32 2^e."""
+    return (2 * H + 4 + 15) // 16 * 16
 
 
 class CudaEpKernels:
@@ -118,6 +124,14 @@ class CudaEpKernels:
                                            nbytes, self._stream()), "gemms_expert_ffn(shared)")
         self._keep = (counts, dest, wts)  # alive until the stream has consumed them
 
+    def pack_back(self, rows):
+        """fp32 [R, H] -> packed combine rows uint8 [R, back_row_bytes(H)]."""
+        R, H = rows.shape
+        packed = torch.empty((max(R, 1), back_row_bytes(H)), dtype=torch.uint8, device=rows.device)
+        _lib.check(self.L.gemms_ep_pack_back(rows.data_ptr(), R, H, packed.data_ptr(), self._stream()),
+                   "gemms_ep_pack_back")
+        return packed[:R]
+
     def combine(self, acc, back, send_row_of, world: int):
         T, H = acc.shape
         out = torch.empty((T, H), dtype=torch.bfloat16, device=acc.device)
@@ -140,12 +154,21 @@ def _cuda_kernels() -> CudaEpKernels:
 @torch.no_grad()
 def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13=None, shared_w13_scale=None,
            shared_w2=None, shared_w2_scale=None, n_group=8, topk_group=4, top_k=8, routed_scaling_factor=2.5,
-           inter_planes=2, logits=None, group=None, kernels=None):
+           inter_planes=2, logits=None, group=None, kernels=None, timeline=None):
     """Expert-parallel layer forward on this rank's tokens ``x`` [T_r, H].
 
     ``w13``/``w2`` (and scales) hold this rank's ``E/W`` experts; the rank's
-    first global expert is ``rank * E/W``.
+    first global expert is ``rank * E/W``.  ``timeline`` (a list) receives
+    ``(phase, torch.cuda.Event)`` pairs recorded on the current stream at the
+    phase boundaries, for per-phase device timing.
     """
+    def mark(name):
+        if timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            timeline.append((name, ev))
+
+    mark("start")
     K = kernels if kernels is not None else _cuda_kernels()
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -158,13 +181,18 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     if logits is None:
         logits = K.router_logits(x, router_w)
     idx, wts = K.route(logits, router_bias, n_group, topk_group, top_k, routed_scaling_factor)
+    mark("router")
     send_counts, send_row_of, send_buf, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local)
+    mark("pack")
 
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     both = torch.stack([send_counts, recv_counts]).cpu()  # the one host synchronisation of the layer
     sc, rc = [int(v) for v in both[0]], [int(v) for v in both[1]]
     S, R = sum(sc), sum(rc)
+    mark("count_exchange")
+    if timeline is not None:
+        timeline.append(("recv_rows", R))
     rb = send_buf.shape[1]
     recv_buf = torch.empty((R, rb), dtype=torch.uint8, device=send_buf.device)
     work = dist.all_to_all_single(recv_buf, send_buf[:S].contiguous(), rc, sc, group=group, async_op=True)
@@ -172,10 +200,18 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
     if shared_w13 is not None:  # overlaps with the dispatch all-to-all
         K.shared_ffn(xq, xq_scale, shared_w13, shared_w13_scale, shared_w2, shared_w2_scale, inter_planes, acc)
+    mark("shared_ffn")
     work.wait()
+    mark("dispatch_wait")
 
     out_rows = K.expert_ffn(recv_buf, R, H, I, top_k, E_local, rank * E_local, inter_planes,
                             w13, w13_scale, w2, w2_scale)
-    back = torch.empty((S, H), dtype=torch.float32, device=x.device)
-    dist.all_to_all_single(back, out_rows.contiguous(), sc, rc, group=group)
-    return K.combine(acc, back, send_row_of, world)
+    mark("expert_ffn")
+    packed = K.pack_back(out_rows)
+    mark("pack_back")
+    back = torch.empty((S, packed.shape[1]), dtype=torch.uint8, device=x.device)
+    dist.all_to_all_single(back, packed.contiguous(), sc, rc, group=group)
+    mark("combine_a2a")
+    out = K.combine(acc, back, send_row_of, world)
+    mark("gather")
+    return out

@@ -159,8 +159,18 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
                         const void* w2, const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
                         gemms_stream_t stream);
 
-/* out bf16 [T, H] = acc fp32 [T, H] + sum over d of back_rows[send_row_of[t, d]]. */
-int gemms_ep_combine(const float* acc, const float* back_rows, const int32_t* send_row_of, int32_t T, int32_t H,
+/* Packed combine row: fp16 [H] holding value / 2^e | fp32 2^e | pad to 16 B,
+ * with 2^e the power of two that puts max|row| / 2^e in [2^14, 2^15) (e = 0
+ * for zero or non-finite rows): the scaling is exact, only fp16 rounding is
+ * added.  Halves the bytes of the combine all-to-all against fp32 rows. */
+size_t gemms_ep_back_row_bytes(int32_t H);
+
+/* out_rows fp32 [R, H] (gemms_ep_expert_ffn) -> packed [R, back_row_bytes]. */
+int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, gemms_stream_t stream);
+
+/* out bf16 [T, H] = acc fp32 [T, H] + sum over d of the packed row
+ * back_packed[send_row_of[t, d]] (fp16 x 2^e), gathered in rank order. */
+int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* send_row_of, int32_t T, int32_t H,
                      int32_t world, void* out_bf16, gemms_stream_t stream);
 
 /* Reads and clears the device error word kept in a gemms_moe_fwd workspace.

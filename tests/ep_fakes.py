@@ -8,6 +8,8 @@ combine mapping -- runs on gloo ranks without a GPU.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from gemms_b200 import ep as EP
@@ -81,11 +83,31 @@ class CpuEpKernels:
     def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes, acc):
         acc += R.shared_expert(R.dequant_hidden(xq, xq_scale), sw13, sw13_scale, sw2, sw2_scale)
 
+    def pack_back(self, rows):
+        """Packed combine rows: fp16 of value / 2^e, then fp32 2^e (``gemms_ep_pack_back``)."""
+        Rn, H = rows.shape
+        packed = torch.zeros((Rn, EP.back_row_bytes(H)), dtype=torch.uint8)
+        for r in range(Rn):
+            amax = float(rows[r].abs().max()) if H else 0.0
+            e = 0
+            if amax > 0 and amax != float("inf") and amax == amax:
+                e = math.frexp(amax)[1] - 15
+            packed[r, :2 * H] = torch.ldexp(rows[r], torch.tensor(-float(e))).to(torch.float16).view(torch.uint8)
+            packed[r, 2 * H:2 * H + 4] = torch.tensor([math.ldexp(1.0, e)], dtype=torch.float32).view(torch.uint8)
+        return packed
+
+    @staticmethod
+    def unpack_back(packed_row, H):
+        vals = packed_row[:2 * H].contiguous().view(torch.float16).to(torch.float32)
+        scale = packed_row[2 * H:2 * H + 4].contiguous().view(torch.float32)[0]
+        return vals * scale
+
     def combine(self, acc, back, send_row_of, world):
         out = acc.clone()
+        H = acc.shape[1]
         for t in range(acc.shape[0]):
             for d in range(world):
                 r = int(send_row_of[t, d])
                 if r >= 0:
-                    out[t] += back[r]
+                    out[t] += self.unpack_back(back[r], H)
         return out.to(torch.bfloat16)

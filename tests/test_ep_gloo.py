@@ -7,6 +7,7 @@ the product code.  The 2-rank result must equal the single-process oracle over
 all tokens.  A second test makes one rank leave before the first collective:
 the remaining rank must raise within its process-group timeout, not hang.
 """
+import math
 import os
 import socket
 import tempfile
@@ -70,8 +71,32 @@ def test_ep_two_ranks_matches_single_process_oracle():
                       d["shared_w13"], d["shared_w13_scale"], d["shared_w2"], d["shared_w2_scale"],
                       n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, rsf=SHAPE.rsf)
     m = R.compare(got, ref)
-    # same fp32 arithmetic, different summation order across ranks
-    assert m["mae_rms"] < 1e-4 and m["max_rel"] < 1e-2, m
+    # Same fp32 arithmetic except the combine rows, which travel as fp16 with
+    # an exact power-of-two scale (2^-11 relative): that flips a few bf16
+    # output roundings (~1e-4 of RMS here).  A misrouted row would cost
+    # errors of the order of the output itself.
+    assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, m
+
+
+def test_pack_back_round_trip():
+    """Packed combine rows: exact power-of-two scale, fp16 rounding only, edge rows."""
+    from tests.ep_fakes import CpuEpKernels
+    g = torch.Generator().manual_seed(0)
+    rows = torch.randn(6, 256, generator=g) * torch.tensor([1e-30, 1e-3, 1.0, 3e4, 1e8, 0.0]).unsqueeze(1)
+    K = CpuEpKernels(1, 1, 1)
+    packed = K.pack_back(rows)
+    assert packed.shape == (6, 2 * 256 + 16)
+    for r in range(6):
+        back = K.unpack_back(packed[r], 256)
+        amax = float(rows[r].abs().max())
+        scale = float(packed[r, 512:516].view(torch.float32)[0])
+        if amax == 0:
+            assert scale == 1.0 and torch.equal(back, rows[r])
+            continue
+        assert 2 ** 14 <= amax / scale < 2 ** 15          # power of two chosen from the row max
+        assert scale == 2.0 ** round(math.log2(scale))
+        err = (back - rows[r]).abs().max() / amax
+        assert err <= 2 ** -11, (r, err)
 
 
 def _leaver_worker(rank, world, port, outdir):

@@ -74,7 +74,11 @@ def test_ep2_matches_single_gpu_and_oracle(case):
         ep = torch.cat([torch.load(os.path.join(tmp, f"ep{r}.pt")) for r in range(world)])
         s = torch.load(os.path.join(tmp, "single.pt"))
     m = R.compare(ep, s["single"])
-    assert m["mae_rms"] < 1e-4 and m["max_rel"] < 5e-3, f"EP vs single GPU: {m}"
+    # The combine rows travel as fp16 with an exact power-of-two scale (2^-11
+    # relative), which flips a few bf16 output roundings against the single-GPU
+    # layer (~1e-4 of RMS); a misrouted row would cost errors of the output's size.
+    assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, f"EP vs single GPU: {m}"
+    print(f"EP2 {case} vs single GPU", m)
     # oracle on a row sample (CPU weights regenerated from the same seed on GPU 0)
     d = W.make_inputs(sh, seed=5, device="cuda:0")
     rows = [0, 1, sh.T // 2, sh.T - 1]
