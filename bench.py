@@ -465,10 +465,11 @@ def gpu_arm(a):
         R = ep_timeline["recv_rows"]
         ffn_bytes = (n_local * 3 * sh.I * sh.H + R * sh.H + 2 * R * planes * 2 * sh.I + 4 * R * sh.H
                      + (3 * sh.I * sh.H + sh.T * sh.H if sh.shared else 0))
-        ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) if sh.shared else 0.0)
+        ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) + ep_timeline.get("shared_ffn_2", 0.0)
+                                              if sh.shared else 0.0)
         ach = ffn_bytes / (ffn_ms / 1e3) / 1e9
         line["roofline"] = {"bound": "hbm", "kernel": "grouped GEMM1+GEMM2 over received rows + shared expert "
-                                                      "(rank 0, expert_ffn + shared_ffn phases)",
+                                                      "(rank 0, expert_ffn + both shared_ffn phases)",
                             "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                             "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else
                             "fallback 6650 GB/s", "traffic": None, "algorithmic_bytes": ffn_bytes,

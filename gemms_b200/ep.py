@@ -14,12 +14,13 @@ expert are replicated.  One layer forward on every rank:
    weights of the experts on the destination;
 3. count exchange (``all_to_all_single`` of int32, then one host read of the
    split sizes) and the dispatch ``all_to_all_single`` of packed rows -- the
-   shared expert runs on the rank's own tokens meanwhile;
+   shared expert runs on the first half of the rank's own tokens meanwhile;
 4. grouped GEMMs over the received rows, each row's result pre-reduced over its
    local experts in fp32;
 5. the rows go back as fp16 with a per-row power-of-two scale (exact
-   scaling, half the bytes of fp32), ``all_to_all_single``, and a
-   deterministic gather-sum per token plus the shared expert, cast to bf16.
+   scaling, half the bytes of fp32), ``all_to_all_single`` while the shared
+   expert runs on the second half of the tokens, and a deterministic
+   gather-sum per token plus the shared expert, cast to bf16.
 
 Every rank issues the same collectives in the same order.  The device work
 goes through a ``kernels`` object: :class:`CudaEpKernels` (the C ABI) by
@@ -108,13 +109,17 @@ class CudaEpKernels:
                                               self._stream()), "gemms_ep_expert_ffn")
         return out[:R]
 
-    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes: int, acc):
-        """acc[T, H] (fp32) += shared expert of the token-major quantised rows."""
+    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes: int, acc, t0: int = 0):
+        """acc[t0 : t0 + n] (fp32) += shared expert of the n token-major quantised
+        rows ``xq`` [n, H] with scales ``xq_scale`` [H/128, n]."""
         T, H = xq.shape
         I = sw2.shape[1]
         dev = xq.device
+        if T == 0:
+            return
+        xq_scale = xq_scale.contiguous()
         counts = torch.full((1,), T, dtype=torch.int32, device=dev)
-        dest = torch.arange(T, dtype=torch.int32, device=dev)
+        dest = torch.arange(t0, t0 + T, dtype=torch.int32, device=dev)
         wts = torch.ones((T,), dtype=torch.float32, device=dev)
         nbytes = self.L.gemms_expert_ffn_workspace_size(T, H, I, 1, planes)
         ws = self._workspace(dev, nbytes, "shared_ffn")
@@ -122,7 +127,7 @@ class CudaEpKernels:
                                            wts.data_ptr(), H, I, 1, planes, sw13.data_ptr(), sw13_scale.data_ptr(),
                                            sw2.data_ptr(), sw2_scale.data_ptr(), acc.data_ptr(), ws.data_ptr(),
                                            nbytes, self._stream()), "gemms_expert_ffn(shared)")
-        self._keep = (counts, dest, wts)  # alive until the stream has consumed them
+        self._keep = getattr(self, "_keep", ())[-4:] + (counts, dest, wts, xq_scale)  # alive until consumed
 
     def pack_back(self, rows):
         """fp32 [R, H] -> packed combine rows uint8 [R, back_row_bytes(H)]."""
@@ -198,8 +203,10 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     work = dist.all_to_all_single(recv_buf, send_buf[:S].contiguous(), rc, sc, group=group, async_op=True)
 
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
-    if shared_w13 is not None:  # overlaps with the dispatch all-to-all
-        K.shared_ffn(xq, xq_scale, shared_w13, shared_w13_scale, shared_w2, shared_w2_scale, inter_planes, acc)
+    T1 = T // 2
+    shared = (shared_w13, shared_w13_scale, shared_w2, shared_w2_scale)
+    if shared_w13 is not None:  # first half of the tokens overlaps the dispatch all-to-all
+        K.shared_ffn(xq[:T1], xq_scale[:, :T1], *shared, inter_planes, acc, 0)
     mark("shared_ffn")
     work.wait()
     mark("dispatch_wait")
@@ -210,7 +217,11 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     packed = K.pack_back(out_rows)
     mark("pack_back")
     back = torch.empty((S, packed.shape[1]), dtype=torch.uint8, device=x.device)
-    dist.all_to_all_single(back, packed.contiguous(), sc, rc, group=group)
+    work = dist.all_to_all_single(back, packed.contiguous(), sc, rc, group=group, async_op=True)
+    if shared_w13 is not None:  # second half of the tokens overlaps the combine all-to-all
+        K.shared_ffn(xq[T1:], xq_scale[:, T1:], *shared, inter_planes, acc, T1)
+    mark("shared_ffn_2")
+    work.wait()
     mark("combine_a2a")
     out = K.combine(acc, back, send_row_of, world)
     mark("gather")

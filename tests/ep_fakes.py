@@ -80,8 +80,11 @@ class CpuEpKernels:
             out.index_add_(0, rows, O * wt.unsqueeze(1))
         return out
 
-    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes, acc):
-        acc += R.shared_expert(R.dequant_hidden(xq, xq_scale), sw13, sw13_scale, sw2, sw2_scale)
+    def shared_ffn(self, xq, xq_scale, sw13, sw13_scale, sw2, sw2_scale, planes, acc, t0=0):
+        n = xq.shape[0]
+        if n:
+            acc[t0:t0 + n] += R.shared_expert(R.dequant_hidden(xq, xq_scale.contiguous()), sw13, sw13_scale, sw2,
+                                              sw2_scale)
 
     def pack_back(self, rows):
         """Packed combine rows: fp16 of value / 2^e, then fp32 2^e (``gemms_ep_pack_back``)."""
