@@ -152,3 +152,30 @@ def test_moe_c1_full_size_sampled_tokens():
     print("c1 sampled parity", m)
     o = out.float()
     assert torch.isfinite(o).all()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("T", [1, 8])
+def test_moe_decode_full_size(T):
+    """Config c2 (decode, full V3 + shared expert): every token checked against
+    the oracle; almost every expert gets 0 or 1 rows, so each M tile is nearly
+    empty and the tile planning / padding rows are exercised."""
+    sh = W.CONFIGS["c2"].replace(T=T)
+    d = W.make_inputs(sh, seed=7, device="cuda")
+    out, idx, w, counts, logits = gemms_b200.moe(
+        d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+        shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
+        shared_w2_scale=d["shared_w2_scale"], return_routing=True)
+    gemms_b200.check_device_errors(tag="moe decode")
+    lg = logits.cpu()
+    bias = d["router_bias"].cpu()
+    ridx, _, _, _ = R.route(lg, bias, 8, 4, 8, 2.5)
+    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
+    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=256))
+    experts = sorted(set(ridx.reshape(-1).tolist()))
+    cw = _cpu_weights_for(d, experts)
+    ref = R.moe_layer(d["x"].cpu(), d["router_w"].cpu(), bias, cw["w13"], cw["w13_scale"], cw["w2"],
+                      cw["w2_scale"], d["shared_w13"].cpu(), d["shared_w13_scale"].cpu(), d["shared_w2"].cpu(),
+                      d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg)
+    m = Hh.assert_parity(out, ref, f"c2 T={T}")
+    print(f"c2 T={T} parity", m)
