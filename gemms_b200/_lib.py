@@ -36,6 +36,7 @@ EXPORTS = (
     "gemms_ep_back_row_bytes",
     "gemms_ep_pack_back",
     "gemms_ep_combine",
+    "gemms_set_gemm_ctas",
 )
 
 
@@ -121,6 +122,8 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                           c_void_p]
         L.gemms_ep_expert_ffn.restype = c_int32
+        L.gemms_set_gemm_ctas.argtypes = [c_int32]
+        L.gemms_set_gemm_ctas.restype = c_int32
         L.gemms_ep_back_row_bytes.argtypes = [c_int32]
         L.gemms_ep_back_row_bytes.restype = c_size_t
         L.gemms_ep_pack_back.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p]

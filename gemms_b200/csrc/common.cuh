@@ -135,5 +135,6 @@ struct Gemm2Args {
 int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
 
 int num_sms();
+int gemm_ctas();  // persistent GEMM grid bound (gemms_set_gemm_ctas)
 
 }  // namespace gemms

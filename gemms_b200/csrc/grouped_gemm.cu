@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#include <atomic>
 #include <cudaTypedefs.h>
 #include <cstdlib>
 #include <mutex>
@@ -536,7 +537,7 @@ int launch_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
     GEMMS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_set = true;
   }
-  const int grid = std::max(1, std::min(num_sms(), max_units));
+  const int grid = std::max(1, std::min(gemm_ctas(), max_units));
   kern<<<grid, kThreads, smem, s>>>(a, b, bs, p);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
@@ -626,6 +627,17 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   return launch_kernel<1, 3, 1>(ma, mb, mbs, p, max_units, s);
 }
 
+// Upper bound on the persistent GEMM grid (0 = one CTA per SM).  The grouped
+// GEMMs hold every SM they get for their whole run, so a collective kernel
+// launched on another stream only progresses on SMs left free; the
+// expert-parallel path lowers the bound while a GEMM overlaps an all-to-all.
+std::atomic<int> g_gemm_cta_limit{0};
+
+int gemm_ctas() {
+  const int lim = g_gemm_cta_limit.load(std::memory_order_relaxed);
+  return lim > 0 ? std::min(lim, num_sms()) : num_sms();
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -639,3 +651,8 @@ int num_sms() {
 }
 
 }  // namespace gemms
+
+extern "C" int gemms_set_gemm_ctas(int32_t max_ctas) {
+  if (max_ctas < 0) return GEMMS_ERR_ARG;
+  return gemms::g_gemm_cta_limit.exchange(max_ctas);
+}

@@ -28,7 +28,9 @@ default; tests pass CPU stand-ins to exercise the exchange logic on gloo ranks.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -68,6 +70,20 @@ class CudaEpKernels:
             self._ws[key] = ws
         off = (-ws.data_ptr()) % 256
         return ws[off:off + nbytes]
+
+    @contextlib.contextmanager
+    def comm_overlap(self):
+        """While active, the persistent grouped GEMMs leave ``GEMMS_EP_COMM_SMS``
+        (default 32) SMs free for the all-to-all running on NCCL's stream; a
+        GEMM given every SM would hold them until it finishes and the
+        collective would wait for it."""
+        reserve = int(os.environ.get("GEMMS_EP_COMM_SMS", "32"))
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        prev = self.L.gemms_set_gemm_ctas(max(1, sms - reserve) if reserve > 0 else 0)
+        try:
+            yield
+        finally:
+            self.L.gemms_set_gemm_ctas(max(prev, 0))
 
     def router_logits(self, x, router_w):
         from .ops import router_logits
@@ -206,7 +222,8 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     T1 = T // 2
     shared = (shared_w13, shared_w13_scale, shared_w2, shared_w2_scale)
     if shared_w13 is not None:  # first half of the tokens overlaps the dispatch all-to-all
-        K.shared_ffn(xq[:T1], xq_scale[:, :T1], *shared, inter_planes, acc, 0)
+        with K.comm_overlap():
+            K.shared_ffn(xq[:T1], xq_scale[:, :T1], *shared, inter_planes, acc, 0)
     mark("shared_ffn")
     work.wait()
     mark("dispatch_wait")
@@ -219,7 +236,8 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     back = torch.empty((S, packed.shape[1]), dtype=torch.uint8, device=x.device)
     work = dist.all_to_all_single(back, packed.contiguous(), sc, rc, group=group, async_op=True)
     if shared_w13 is not None:  # second half of the tokens overlaps the combine all-to-all
-        K.shared_ffn(xq[T1:], xq_scale[:, T1:], *shared, inter_planes, acc, T1)
+        with K.comm_overlap():
+            K.shared_ffn(xq[T1:], xq_scale[:, T1:], *shared, inter_planes, acc, T1)
     mark("shared_ffn_2")
     work.wait()
     mark("combine_a2a")

@@ -173,6 +173,14 @@ int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, ge
 int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* send_row_of, int32_t T, int32_t H,
                      int32_t world, void* out_bf16, gemms_stream_t stream);
 
+/* Bounds the grid of the persistent grouped-GEMM kernels to max_ctas CTAs
+ * (0 = one per SM, the default) for launches made after the call, from any
+ * thread.  Returns the previous bound, or GEMMS_ERR_ARG for a negative value.
+ * The GEMMs keep every SM they are given for their whole run, so a collective
+ * on another stream (the expert-parallel all-to-alls) only progresses on SMs
+ * left free.  No counterpart in the reference. */
+int gemms_set_gemm_ctas(int32_t max_ctas);
+
 /* Reads and clears the device error word kept in a gemms_moe_fwd workspace.
  * Synchronises the stream.  *flags receives the raw bit set (0 = clean). */
 int gemms_moe_check(void* workspace, gemms_stream_t stream, int32_t* flags);

@@ -8,6 +8,7 @@ combine mapping -- runs on gloo ranks without a GPU.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -21,6 +22,9 @@ BLOCK = 128
 class CpuEpKernels:
     def __init__(self, n_group, topk_group, top_k):
         self.ng, self.tg, self.k = n_group, topk_group, top_k
+
+    def comm_overlap(self):
+        return contextlib.nullcontext()
 
     def router_logits(self, x, router_w):
         return R.router_logits(x, router_w)

@@ -179,3 +179,26 @@ def test_moe_decode_full_size(T):
                       d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg)
     m = Hh.assert_parity(out, ref, f"c2 T={T}")
     print(f"c2 T={T} parity", m)
+
+
+def test_gemm_cta_bound_keeps_results():
+    """gemms_set_gemm_ctas: the persistent GEMMs stride their work units over
+    however many CTAs they get; a small grid gives the same layer output (up to
+    the order of the fp32 combine atomics)."""
+    from gemms_b200 import _lib
+    L = _lib.load()
+    sh = W.CONFIGS["c0"].replace(shared=True)
+    d = Hh.to_dev(W.make_inputs(sh, seed=4))
+    args = (d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"])
+    kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
+              **{k: d[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale")})
+    full = gemms_b200.moe(*args, **kw).float()
+    assert L.gemms_set_gemm_ctas(-1) == -8  # GEMMS_ERR_ARG
+    prev = L.gemms_set_gemm_ctas(5)
+    try:
+        small = gemms_b200.moe(*args, **kw).float()
+        torch.cuda.synchronize()
+    finally:
+        assert L.gemms_set_gemm_ctas(prev) == 5
+    gemms_b200.check_device_errors(tag="cta bound")
+    assert (small - full).norm() <= 1e-3 * full.norm()
