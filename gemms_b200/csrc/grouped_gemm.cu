@@ -164,7 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_holder;
+  // The TMEM base address is re-read from shared memory inside each role:
+  // a value kept live across the role split was spilled to local memory and
+  // reloaded once per K block by every epilogue warp and the MMA thread.
 
   const int num_tiles = min(*p.num_tiles, p.max_tiles);
   const int total = num_tiles * p.n_tiles;
@@ -252,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int pl = 0; pl < PLANES; ++pl) da[s][pl] = smem_desc_k_sw128(smem_u32(st + pl * kTileA));
         db[s] = smem_desc_k_sw128(smem_u32(st + PLANES * kTileA));
       }
+      const uint32_t tmem_d = *reinterpret_cast<volatile const uint32_t*>(tmem_holder);
       int it = 0, acc_it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem_base + buf * BN;
+          const uint32_t d = tmem_d + buf * BN;
           uint64_t bd = db[0];
           uint64_t ad[PLANES];
 #pragma unroll
@@ -303,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;         // TMEM lane quadrant this warp may access
     const int h = ew >> 2;          // column half
     const int r = q * 32 + lane;    // row within the tile
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t lane_base =
+        *reinterpret_cast<volatile const uint32_t*>(tmem_holder) + (static_cast<uint32_t>(q * 32) << 16);
     const int wblk = p.w_rows / kBlock;
     int acc_it = 0, unit_i = 0;
     bool ok = true;
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(*reinterpret_cast<volatile const uint32_t*>(tmem_holder), kTmemCols);
   }
 }
 
