@@ -66,3 +66,43 @@ def test_operators_refuse_cpu_tensors():
         gemms_b200.moe(x, torch.zeros(8, 256), torch.zeros(8), torch.zeros(8, 256, 256).to(torch.float8_e4m3fn),
                        torch.ones(8, 2, 2), torch.zeros(8, 256, 128).to(torch.float8_e4m3fn), torch.ones(8, 2, 1),
                        n_group=4, topk_group=2, top_k=2)
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """include/gemms_moe.h is a C header: a C99 program that includes it links
+    against the library and calls the host-only entry points (no GPU needed)."""
+    import shutil
+    import subprocess
+    from gemms_b200 import build as B
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "abi.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "gemms_moe.h"
+int main(void) {
+  GemmsMoeShape s;
+  memset(&s, 0, sizeof s);
+  s.T = 4096; s.H = 7168; s.I = 2048; s.E = 256; s.E_local = 256; s.n_group = 8; s.topk_group = 4;
+  s.top_k = 8; s.has_shared = 1; s.input_mode = GEMMS_INPUT_BF16; s.inter_planes = 2;
+  s.routed_scaling_factor = 2.5f;
+  size_t n = gemms_moe_workspace_size(&s);
+  s.H = 7000;  /* not a multiple of 128: rejected */
+  size_t bad = gemms_moe_workspace_size(&s);
+  printf("%zu %zu %d\n%s\n", n, bad, gemms_moe_fwd(NULL, NULL, 0, NULL), gemms_version());
+  return (n > 0 && bad == 0) ? 0 : 1;
+}
+""")
+    exe = tmp_path / "abi"
+    libdir = os.path.dirname(B.LIB)
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(root, "include"), str(src), "-o",
+                        str(exe), "-L", libdir, "-lgemms_b200", "-Wl,-rpath," + libdir], capture_output=True,
+                       text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout + out.stderr
+    n, bad, rc = out.stdout.splitlines()[0].split()
+    assert int(n) > 0 and int(bad) == 0 and int(rc) == -8  # GEMMS_ERR_ARG for NULL args
