@@ -63,7 +63,7 @@ class CudaEpKernels:
         return torch.cuda.current_stream().cuda_stream
 
     def _workspace(self, dev, nbytes: int, tag: str) -> torch.Tensor:
-        key = (dev.index, tag)
+        key = (dev.index, torch.cuda.current_stream(dev).cuda_stream, tag)  # per stream: no sharing across streams
         ws = self._ws.get(key)
         if ws is None or ws.numel() < nbytes + 256:
             ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)

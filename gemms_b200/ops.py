@@ -43,8 +43,11 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
-    """Per (device, tag) workspace from torch's caching allocator, grown on demand."""
-    key = (device.index, tag)
+    """Per (device, stream, tag) workspace from torch's caching allocator, grown
+    on demand.  Keyed by stream so that layers running concurrently on
+    different streams never share scratch; a replaced workspace is freed on
+    the stream it was allocated on, so the allocator reuses it in stream order."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream, tag)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 256) + 256, dtype=torch.uint8, device=device)
@@ -87,7 +90,7 @@ def check_device_errors(ws: torch.Tensor | None = None, tag: str = "moe") -> Non
     L = _lib.load()
     if ws is None:
         dev = torch.cuda.current_device()
-        cached = _workspaces.get((dev, tag))
+        cached = _workspaces.get((dev, torch.cuda.current_stream(dev).cuda_stream, tag))
         if cached is None:
             return
         ws = cached[(-cached.data_ptr()) % 256:]

@@ -202,3 +202,27 @@ def test_gemm_cta_bound_keeps_results():
         assert L.gemms_set_gemm_ctas(prev) == 5
     gemms_b200.check_device_errors(tag="cta bound")
     assert (small - full).norm() <= 1e-3 * full.norm()
+
+
+def test_concurrent_streams_do_not_share_scratch():
+    """Layers launched on two streams at once (each with its own inputs) give
+    what they give when run one after the other."""
+    sh = W.CONFIGS["c0"].replace(shared=True)
+    d = Hh.to_dev(W.make_inputs(sh, seed=9))
+    kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
+              **{k: d[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale")})
+    wts = (d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"])
+    xs = [d["x"], (d["x"].float() * -0.5).to(torch.bfloat16)]
+    serial = [gemms_b200.moe(x, *wts, **kw).float() for x in xs]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [None, None]
+    for _ in range(3):
+        for i, st in enumerate(streams):
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                outs[i] = gemms_b200.moe(xs[i], *wts, **kw)
+        torch.cuda.synchronize()
+        for i in range(2):
+            o = outs[i].float()
+            assert (o - serial[i]).norm() <= 1e-3 * serial[i].norm(), f"stream {i}"
