@@ -536,10 +536,15 @@ int launch_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
                   int max_units, cudaStream_t s) {
   auto kern = grouped_gemm_kernel<MODE, PLANES, OUT_PLANES>;
   constexpr int smem = Cfg<PLANES>::kSmemBytes;
-  static bool attr_set = false;  // per template instance; the attribute is per device function
-  if (!attr_set) {
+  // The shared-memory opt-in is per device: one bit per device (per template
+  // instance) that has been given it.
+  static std::atomic<unsigned long long> attr_set{0};
+  int dev = 0;
+  GEMMS_CUDA_TRY(cudaGetDevice(&dev));
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (!bit || !(attr_set.load(std::memory_order_relaxed) & bit)) {
     GEMMS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
+    attr_set.fetch_or(bit, std::memory_order_relaxed);
   }
   const int grid = std::max(1, std::min(gemm_ctas(), max_units));
   kern<<<grid, kThreads, smem, s>>>(a, b, bs, p);

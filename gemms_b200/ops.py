@@ -17,6 +17,7 @@ no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import functools
 
 import torch
 
@@ -33,6 +34,21 @@ class ShapeError(ValueError, AssertionError):
 def _req(cond: bool, msg: str) -> None:
     if not cond:
         raise ShapeError(msg)
+
+
+def _on_tensor_device(fn):
+    """Runs the operator with its first CUDA tensor argument's device current,
+    so that kernels go to that device's current stream (not to whichever
+    device the caller left current, which would be handed another GPU's
+    pointers)."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        for v in list(args) + list(kwargs.values()):
+            if isinstance(v, torch.Tensor) and v.is_cuda:
+                with torch.cuda.device(v.device):
+                    return fn(*args, **kwargs)
+        return fn(*args, **kwargs)
+    return wrapper
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -101,6 +117,7 @@ def check_device_errors(ws: torch.Tensor | None = None, tag: str = "moe") -> Non
 
 
 @torch.no_grad()
+@_on_tensor_device
 def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states: torch.Tensor,
         hidden_states_scale: torch.Tensor, gemm1_weights: torch.Tensor, gemm1_weights_scale: torch.Tensor,
         gemm2_weights: torch.Tensor, gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
@@ -159,6 +176,7 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     return out
 
 
+@_on_tensor_device
 def router_logits(x: torch.Tensor, router_w: torch.Tensor) -> torch.Tensor:
     """fp32 logits = x . router_w^T from a bf16 x and an fp32 router weight.
 
@@ -175,6 +193,7 @@ def router_logits(x: torch.Tensor, router_w: torch.Tensor) -> torch.Tensor:
 
 
 @torch.no_grad()
+@_on_tensor_device
 def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13: torch.Tensor,
         w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor, *,
         shared_w13: torch.Tensor | None = None, shared_w13_scale: torch.Tensor | None = None,
@@ -252,6 +271,7 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
 
 
 @torch.no_grad()
+@_on_tensor_device
 def route(logits: torch.Tensor, bias: torch.Tensor, *, n_group: int, topk_group: int, top_k: int,
           routed_scaling_factor: float = 2.5, counts: bool = True):
     """CUDA router only: returns (topk_idx int32 [T,k], topk_w fp32 [T,k], counts int32 [E])."""

@@ -52,6 +52,10 @@ class MoePipeline:
         """
         if len(host_x) != len(host_y):
             raise ValueError("host_x and host_y must have the same length")
+        with torch.cuda.device(self.dev):
+            self._run(host_x, host_y)
+
+    def _run(self, host_x, host_y):
         compute = torch.cuda.current_stream(self.dev)
         for i, (xh, yh) in enumerate(zip(host_x, host_y)):
             k = i % self.slots

@@ -226,3 +226,25 @@ def test_concurrent_streams_do_not_share_scratch():
         for i in range(2):
             o = outs[i].float()
             assert (o - serial[i]).norm() <= 1e-3 * serial[i].norm(), f"stream {i}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_second_device_in_one_process():
+    """One process, two GPUs: the layer on cuda:1 tensors while cuda:0 is the
+    current device runs on cuda:1 (kernels go to the tensors' device) and
+    matches the same layer on cuda:0 (each device gets the GEMMs' shared-memory
+    opt-in)."""
+    sh = W.CONFIGS["c0"].replace(shared=True)
+    cpu = W.make_inputs(sh, seed=6)
+    kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf)
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        d = Hh.to_dev(cpu, dev)
+        torch.cuda.set_device(0)
+        out = gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                             d["w2_scale"], shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"],
+                             shared_w2=d["shared_w2"], shared_w2_scale=d["shared_w2_scale"], **kw)
+        assert out.device == torch.device(dev)
+        torch.cuda.synchronize(dev)
+        outs.append(out.float().cpu())
+    assert (outs[1] - outs[0]).norm() <= 1e-3 * outs[0].norm()
