@@ -49,6 +49,8 @@ def _args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
+    p.add_argument("--ep-combine", choices=["nccl", "peer"], default=None,
+                   help="N>1: combine through NCCL all-to-all (default) or peer reads of symmetric buffers")
     return p.parse_args()
 
 
@@ -275,6 +277,8 @@ def count_kernels_per_step(step_fn) -> int:
 
 
 def gpu_arm(a):
+    if a.ep_combine:
+        os.environ["GEMMS_EP_COMBINE"] = a.ep_combine
     import torch
     import torch.distributed as dist
 
@@ -451,6 +455,7 @@ def gpu_arm(a):
                                     + (" + shared expert" if sh.shared else "")),
                        "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
                        "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                       **({"ep_combine": os.environ.get("GEMMS_EP_COMBINE", "nccl")} if world > 1 else {}),
                        "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"},
             "tflops": flops / (ms / 1e3) / 1e12,
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,

@@ -36,6 +36,7 @@ EXPORTS = (
     "gemms_ep_back_row_bytes",
     "gemms_ep_pack_back",
     "gemms_ep_combine",
+    "gemms_ep_combine_rows",
     "gemms_set_gemm_ctas",
 )
 
@@ -129,6 +130,9 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_ep_pack_back.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p]
         L.gemms_ep_pack_back.restype = c_int32
         L.gemms_ep_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
+        L.gemms_ep_combine_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                            c_void_p, c_void_p]
+        L.gemms_ep_combine_rows.restype = c_int32
         L.gemms_ep_combine.restype = c_int32
         _lib = L
         return L

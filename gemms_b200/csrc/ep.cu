@@ -227,26 +227,33 @@ __global__ void __launch_bounds__(256) ep_pack_back_kernel(const float* __restri
   if (threadIdx.x == 0) *reinterpret_cast<float*>(dst + 2 * (size_t)H) = ldexpf(1.0f, x);
 }
 
-__global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc,
-                                                         const uint8_t* __restrict__ back, size_t rbb,
-                                                         const int32_t* __restrict__ send_row_of, int T, int H,
-                                                         int world, __nv_bfloat16* __restrict__ out) {
+// Where each destination's packed combine rows live: row (send_row_of[t, d] +
+// add[d]) of the buffer at base[d].  One buffer for the all-to-all path;
+// each rank's own buffer (peer pointers, read over NVLink) for the peer path.
+struct BackRows {
+  const uint8_t* base[kMaxWorld];
+  int add[kMaxWorld];
+};
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc, const BackRows rows_at,
+                                                         size_t rbb, const int32_t* __restrict__ send_row_of, int T,
+                                                         int H, int world, __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
-  int rows[kMaxWorld];
+  const uint8_t* rows[kMaxWorld];
   float scale[kMaxWorld];
   int nd = 0;
   for (int d = 0; d < world; ++d) {
     const int r = send_row_of[(size_t)t * world + d];
     if (r >= 0) {
-      rows[nd] = r;
-      scale[nd] = *reinterpret_cast<const float*>(back + (size_t)r * rbb + 2 * (size_t)H);
+      rows[nd] = rows_at.base[d] + (size_t)(r + rows_at.add[d]) * rbb;
+      scale[nd] = *reinterpret_cast<const float*>(rows[nd] + 2 * (size_t)H);
       ++nd;
     }
   }
   for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
     float4 s = *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
     for (int i = 0; i < nd; ++i) {
-      const uint2 b = *reinterpret_cast<const uint2*>(back + (size_t)rows[i] * rbb + 2 * (size_t)c);
+      const uint2 b = *reinterpret_cast<const uint2*>(rows[i] + 2 * (size_t)c);
       const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
       const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
       s.x = fmaf(lo.x, scale[i], s.x);
@@ -480,9 +487,29 @@ int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* s
   if (!acc || !send_row_of || !out_bf16) return GEMMS_ERR_ARG;  // back_packed may be NULL when nothing was sent
   if (!aligned16(acc) || !aligned16(out_bf16) || (back_packed && !aligned16(back_packed))) return GEMMS_ERR_ALIGN;
   if (T == 0) return GEMMS_OK;
+  BackRows at{};
+  for (int d = 0; d < world; ++d) at.base[d] = static_cast<const uint8_t*>(back_packed);
   ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      acc, static_cast<const uint8_t*>(back_packed), ep_back_row_bytes(H), send_row_of, T, H, world,
-      static_cast<__nv_bfloat16*>(out_bf16));
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_ep_combine_rows(const float* acc, const void* const* row_base, const int32_t* row_add,
+                          const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, void* out_bf16,
+                          gemms_stream_t stream_) {
+  if (T < 0 || H <= 0 || H % 4 || world < 1 || world > kMaxWorld) return GEMMS_ERR_SHAPE;
+  if (!acc || !send_row_of || !out_bf16 || !row_base || !row_add) return GEMMS_ERR_ARG;
+  if (!aligned16(acc) || !aligned16(out_bf16)) return GEMMS_ERR_ALIGN;
+  if (T == 0) return GEMMS_OK;
+  BackRows at{};
+  for (int d = 0; d < world; ++d) {
+    if (row_base[d] && !aligned16(row_base[d])) return GEMMS_ERR_ALIGN;
+    at.base[d] = static_cast<const uint8_t*>(row_base[d]);
+    at.add[d] = row_add[d];
+  }
+  ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

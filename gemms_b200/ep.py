@@ -57,6 +57,7 @@ class CudaEpKernels:
     def __init__(self):
         self.L = _lib.load()
         self._ws = {}
+        self._symm = {}
 
     @staticmethod
     def _stream() -> int:
@@ -145,13 +146,69 @@ class CudaEpKernels:
                                            nbytes, self._stream()), "gemms_expert_ffn(shared)")
         self._keep = getattr(self, "_keep", ())[-4:] + (counts, dest, wts, xq_scale)  # alive until consumed
 
-    def pack_back(self, rows):
-        """fp32 [R, H] -> packed combine rows uint8 [R, back_row_bytes(H)]."""
+    def pack_back(self, rows, out=None):
+        """fp32 [R, H] -> packed combine rows uint8 [R, back_row_bytes(H)] (into
+        the front of the flat uint8 buffer ``out`` when given)."""
         R, H = rows.shape
-        packed = torch.empty((max(R, 1), back_row_bytes(H)), dtype=torch.uint8, device=rows.device)
+        if out is None:
+            packed = torch.empty((max(R, 1), back_row_bytes(H)), dtype=torch.uint8, device=rows.device)
+        else:
+            if out.numel() < R * back_row_bytes(H):
+                raise ValueError("pack_back: output buffer too small")
+            packed = out[:max(R, 1) * back_row_bytes(H)].view(max(R, 1), back_row_bytes(H))
         _lib.check(self.L.gemms_ep_pack_back(rows.data_ptr(), R, H, packed.data_ptr(), self._stream()),
                    "gemms_ep_pack_back")
         return packed[:R]
+
+    # ---- peer-memory combine (GEMMS_EP_COMBINE=peer) --------------------
+    def peer_buffers(self, group, cap_rows: int, H: int):
+        """This rank's half of a double-buffered symmetric allocation for packed
+        combine rows and every rank's address of it (peer pointers, mapped into
+        this process).  Calls alternate between the two buffers: a rank writes
+        buffer i % 2 only after the barrier of call i - 1, which every rank
+        passes only once it has finished reading buffer (i - 2) % 2.  Grows
+        (collectively: ``cap_rows`` is the same on every rank) when needed."""
+        import torch.distributed._symmetric_memory as symm_mem
+        g = group if group is not None else dist.group.WORLD
+        rbb = back_row_bytes(H)
+        need = max(cap_rows, 1) * rbb
+        st = self._symm.get(g.group_name)
+        if st is None or st["bytes"] < need:
+            if st is not None:  # peers may still read the old buffers: barrier, then drain before freeing
+                self.peer_publish(g, None, None)
+                torch.cuda.current_stream().synchronize()
+            nbytes = -(-need * 5 // 4 // (1 << 20)) * (1 << 20)  # 25% headroom, whole MiB
+            dev = torch.device("cuda", torch.cuda.current_device())
+            bufs, ptrs, hdls = [], [], []
+            for _ in range(2):
+                b = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+                h = symm_mem.rendezvous(b, g)
+                bufs.append(b)
+                hdls.append(h)
+                ptrs.append([int(p) for p in h.buffer_ptrs])
+            st = {"bytes": nbytes, "bufs": bufs, "ptrs": ptrs, "hdls": hdls, "parity": 0}
+            self._symm[g.group_name] = st
+        i = st["parity"]
+        st["parity"] ^= 1
+        return st["bufs"][i], st["ptrs"][i]
+
+    def peer_publish(self, group, local, peers):
+        """Barrier: every rank's writes of its buffer are complete (a one-element
+        NCCL all-reduce, ordered after them on each rank's stream)."""
+        tok = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(tok, group=group)
+        return peers
+
+    def combine_rows(self, acc, peers, row_add, send_row_of, world: int):
+        """out bf16 [T, H] = acc + the packed rows read in place from each
+        destination's buffer (``gemms_ep_combine_rows``)."""
+        T, H = acc.shape
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=acc.device)
+        bases = (ctypes.c_void_p * world)(*peers)
+        adds = (ctypes.c_int32 * world)(*row_add)
+        _lib.check(self.L.gemms_ep_combine_rows(acc.data_ptr(), bases, adds, send_row_of.data_ptr(), T, H, world,
+                                                out.data_ptr(), self._stream()), "gemms_ep_combine_rows")
+        return out
 
     def combine(self, acc, back, send_row_of, world: int):
         T, H = acc.shape
@@ -175,13 +232,19 @@ def _cuda_kernels() -> CudaEpKernels:
 @torch.no_grad()
 def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13=None, shared_w13_scale=None,
            shared_w2=None, shared_w2_scale=None, n_group=8, topk_group=4, top_k=8, routed_scaling_factor=2.5,
-           inter_planes=2, logits=None, group=None, kernels=None, timeline=None):
+           inter_planes=2, logits=None, group=None, kernels=None, timeline=None, combine=None):
     """Expert-parallel layer forward on this rank's tokens ``x`` [T_r, H].
 
     ``w13``/``w2`` (and scales) hold this rank's ``E/W`` experts; the rank's
     first global expert is ``rank * E/W``.  ``timeline`` (a list) receives
     ``(phase, torch.cuda.Event)`` pairs recorded on the current stream at the
     phase boundaries, for per-phase device timing.
+
+    ``combine`` (default: ``GEMMS_EP_COMBINE``, else ``"nccl"``) picks how the
+    result rows come back: ``"nccl"`` sends them with ``all_to_all_single``;
+    ``"peer"`` leaves them in a symmetric (NVLink-mapped) buffer on the rank
+    that computed them and the combine kernel of the token's own rank reads
+    them from there, after one barrier.
     """
     def mark(name):
         if timeline is not None:
@@ -190,6 +253,9 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
             timeline.append((name, ev))
 
     mark("start")
+    combine = combine or os.environ.get("GEMMS_EP_COMBINE", "nccl")
+    if combine not in ("nccl", "peer"):
+        raise ValueError(f"combine must be 'nccl' or 'peer', not {combine!r}")
     K = kernels if kernels is not None else _cuda_kernels()
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -206,10 +272,13 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     send_counts, send_row_of, send_buf, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local)
     mark("pack")
 
-    recv_counts = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv_counts, send_counts, group=group)
-    both = torch.stack([send_counts, recv_counts]).cpu()  # the one host synchronisation of the layer
-    sc, rc = [int(v) for v in both[0]], [int(v) for v in both[1]]
+    # count matrix m[src, dst] on every rank: this rank's send and receive
+    # counts, and (peer combine) where its rows sit in each destination's order
+    gathered = [torch.empty_like(send_counts) for _ in range(world)]
+    dist.all_gather(gathered, send_counts, group=group)
+    m = torch.stack(gathered).cpu().tolist()  # the one host synchronisation of the layer
+    sc = [int(v) for v in m[rank]]
+    rc = [int(m[src][rank]) for src in range(world)]
     S, R = sum(sc), sum(rc)
     mark("count_exchange")
     if timeline is not None:
@@ -219,7 +288,9 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     work = dist.all_to_all_single(recv_buf, send_buf[:S].contiguous(), rc, sc, group=group, async_op=True)
 
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
-    T1 = T // 2
+    # With the all-to-all combine the shared expert is split so that its second
+    # half hides that collective; the peer combine has no collective to hide.
+    T1 = T // 2 if combine == "nccl" else T
     shared = (shared_w13, shared_w13_scale, shared_w2, shared_w2_scale)
     if shared_w13 is not None:  # first half of the tokens overlaps the dispatch all-to-all
         with K.comm_overlap():
@@ -231,6 +302,18 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     out_rows = K.expert_ffn(recv_buf, R, H, I, top_k, E_local, rank * E_local, inter_planes,
                             w13, w13_scale, w2, w2_scale)
     mark("expert_ffn")
+    if combine == "peer":
+        send_off = [sum(sc[:d]) for d in range(world)]
+        row_add = [sum(int(m[src][d]) for src in range(rank)) - send_off[d] for d in range(world)]
+        cap = max(sum(int(m[src][d]) for src in range(world)) for d in range(world))
+        local, peers = K.peer_buffers(group, cap, H)
+        K.pack_back(out_rows, out=local)
+        mark("pack_back")
+        peers = K.peer_publish(group, local, peers)
+        mark("publish")
+        out = K.combine_rows(acc, peers, row_add, send_row_of, world)
+        mark("gather")
+        return out
     packed = K.pack_back(out_rows)
     mark("pack_back")
     back = torch.empty((S, packed.shape[1]), dtype=torch.uint8, device=x.device)

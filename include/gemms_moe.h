@@ -173,6 +173,18 @@ int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, ge
 int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* send_row_of, int32_t T, int32_t H,
                      int32_t world, void* out_bf16, gemms_stream_t stream);
 
+/* As gemms_ep_combine, but destination d's packed rows are read in place: the
+ * row for (t, d) is row send_row_of[t, d] + row_add[d] of the buffer at
+ * row_base[d] (host arrays of `world` entries; 16-byte aligned device
+ * addresses, which may be other GPUs' memory mapped into this process, e.g.
+ * the peer pointers of a symmetric allocation, read over NVLink).  The caller
+ * guarantees that every row read lies inside its buffer, that its writers
+ * have finished before this call's kernel starts, and that they do not write
+ * it again until the kernel has completed.  No counterpart in the reference. */
+int gemms_ep_combine_rows(const float* acc, const void* const* row_base, const int32_t* row_add,
+                          const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, void* out_bf16,
+                          gemms_stream_t stream);
+
 /* Bounds the grid of the persistent grouped-GEMM kernels to max_ctas CTAs
  * (0 = one per SM, the default) for launches made after the call, from any
  * thread.  Returns the previous bound, or GEMMS_ERR_ARG for a negative value.

@@ -90,10 +90,13 @@ class CpuEpKernels:
             acc[t0:t0 + n] += R.shared_expert(R.dequant_hidden(xq, xq_scale.contiguous()), sw13, sw13_scale, sw2,
                                               sw2_scale)
 
-    def pack_back(self, rows):
+    def pack_back(self, rows, out=None):
         """Packed combine rows: fp16 of value / 2^e, then fp32 2^e (``gemms_ep_pack_back``)."""
         Rn, H = rows.shape
-        packed = torch.zeros((Rn, EP.back_row_bytes(H)), dtype=torch.uint8)
+        if out is None:
+            packed = torch.zeros((Rn, EP.back_row_bytes(H)), dtype=torch.uint8)
+        else:
+            packed = out[:Rn * EP.back_row_bytes(H)].view(Rn, EP.back_row_bytes(H))
         for r in range(Rn):
             amax = float(rows[r].abs().max()) if H else 0.0
             e = 0
@@ -102,6 +105,31 @@ class CpuEpKernels:
             packed[r, :2 * H] = torch.ldexp(rows[r], torch.tensor(-float(e))).to(torch.float16).view(torch.uint8)
             packed[r, 2 * H:2 * H + 4] = torch.tensor([math.ldexp(1.0, e)], dtype=torch.float32).view(torch.uint8)
         return packed
+
+    # peer combine: each rank's buffer stands for its symmetric allocation; the
+    # "barrier" hands every rank a copy of all buffers (gloo all_gather), and
+    # the combine reads rows from them with the offsets moe_ep computed.
+    def peer_buffers(self, group, cap_rows, H):
+        local = torch.zeros(max(cap_rows, 1) * EP.back_row_bytes(H), dtype=torch.uint8)
+        return local, None
+
+    def peer_publish(self, group, local, peers):
+        import torch.distributed as dist
+        bufs = [torch.empty_like(local) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(bufs, local, group=group)
+        return bufs
+
+    def combine_rows(self, acc, peers, row_add, send_row_of, world):
+        out = acc.clone()
+        H = acc.shape[1]
+        rbb = EP.back_row_bytes(H)
+        for t in range(acc.shape[0]):
+            for d in range(world):
+                r = int(send_row_of[t, d])
+                if r >= 0:
+                    row = peers[d].view(-1, rbb)[r + row_add[d]]
+                    out[t] += self.unpack_back(row, H)
+        return out.to(torch.bfloat16)
 
     @staticmethod
     def unpack_back(packed_row, H):

@@ -37,7 +37,7 @@ def _inputs():
     return W.make_inputs(SHAPE, seed=4)
 
 
-def _ep_worker(rank, world, port, outdir):
+def _ep_worker(rank, world, port, outdir, combine="nccl"):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from tests.ep_fakes import CpuEpKernels
@@ -55,16 +55,18 @@ def _ep_worker(rank, world, port, outdir):
                     d["w2_scale"][el], shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"],
                     shared_w2=d["shared_w2"], shared_w2_scale=d["shared_w2_scale"], n_group=SHAPE.n_group,
                     topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, routed_scaling_factor=SHAPE.rsf,
-                    group=dist.group.WORLD, kernels=K)
+                    group=dist.group.WORLD, kernels=K, combine=combine)
     torch.save(out, os.path.join(outdir, f"out{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_ep_two_ranks_matches_single_process_oracle():
-    world = 2
+@pytest.mark.parametrize("combine,world", [("nccl", 2), ("peer", 2), ("nccl", 4), ("peer", 4)])
+def test_ep_ranks_match_single_process_oracle(combine, world):
+    """Both combine modes: the all-to-all, and the peer read of rows left on
+    the rank that computed them (row offsets from the count matrix)."""
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_ep_worker, args=(world, _free_port(), tmp), nprocs=world, join=True)
+        mp.spawn(_ep_worker, args=(world, _free_port(), tmp, combine), nprocs=world, join=True)
         got = torch.cat([torch.load(os.path.join(tmp, f"out{r}.pt")) for r in range(world)])
     d = _inputs()
     ref = R.moe_layer(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],

@@ -28,8 +28,9 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, outdir, case):
+def _worker(rank, world, port, outdir, case, combine="nccl"):
     import sys
+    os.environ["GEMMS_EP_COMBINE"] = combine
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import gemms_b200
 
@@ -62,15 +63,17 @@ def _worker(rank, world, port, outdir, case):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("case", ["c0", "v3"])
-def test_ep2_matches_single_gpu_and_oracle(case):
+@pytest.mark.parametrize("case,combine", [("c0", "nccl"), ("v3", "nccl"), ("c0", "peer"), ("v3", "peer")])
+def test_ep2_matches_single_gpu_and_oracle(case, combine):
+    """Both combine modes; "peer" reads the result rows from the other GPU's
+    symmetric buffer over NVLink."""
     from oracle import reference_moe as R
     from tests import helpers as Hh
 
     world = 2
     sh = CASES[case]
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_worker, args=(world, _free_port(), tmp, case), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), tmp, case, combine), nprocs=world, join=True)
         ep = torch.cat([torch.load(os.path.join(tmp, f"ep{r}.pt")) for r in range(world)])
         s = torch.load(os.path.join(tmp, "single.pt"))
     m = R.compare(ep, s["single"])
@@ -78,7 +81,7 @@ def test_ep2_matches_single_gpu_and_oracle(case):
     # relative), which flips a few bf16 output roundings against the single-GPU
     # layer (~1e-4 of RMS); a misrouted row would cost errors of the output's size.
     assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, f"EP vs single GPU: {m}"
-    print(f"EP2 {case} vs single GPU", m)
+    print(f"EP2 {case} {combine} vs single GPU", m)
     # oracle on a row sample (CPU weights regenerated from the same seed on GPU 0)
     d = W.make_inputs(sh, seed=5, device="cuda:0")
     rows = [0, 1, sh.T // 2, sh.T - 1]
