@@ -106,3 +106,22 @@ int main(void) {
     assert out.returncode == 0, out.stdout + out.stderr
     n, bad, rc = out.stdout.splitlines()[0].split()
     assert int(n) > 0 and int(bad) == 0 and int(rc) == -8  # GEMMS_ERR_ARG for NULL args
+
+
+def test_new_entry_points_validate_arguments_without_gpu():
+    """Argument checks of the expert-parallel combine entry points and the GEMM
+    grid bound run on the host, before any CUDA call."""
+    L = _lib.load()
+    ERR_SHAPE, ERR_ARG = -1, -8  # GEMMS_ERR_SHAPE, GEMMS_ERR_ARG
+    assert L.gemms_ep_back_row_bytes(7168) == 2 * 7168 + 16
+    assert L.gemms_ep_back_row_bytes(0) == 0
+    assert L.gemms_ep_pack_back(None, 0, 7168, None, None) == 0            # nothing to pack
+    assert L.gemms_ep_pack_back(None, 4, 7168, None, None) == ERR_ARG
+    assert L.gemms_ep_pack_back(None, 4, 7166, None, None) == ERR_SHAPE
+    bases = (ctypes.c_void_p * 2)(None, None)
+    adds = (ctypes.c_int32 * 2)(0, 0)
+    assert L.gemms_ep_combine_rows(None, bases, adds, None, 4, 7168, 2, None, None) == ERR_ARG
+    assert L.gemms_ep_combine_rows(None, bases, adds, None, 4, 7168, 33, None, None) == ERR_SHAPE
+    assert L.gemms_set_gemm_ctas(-1) == ERR_ARG
+    prev = L.gemms_set_gemm_ctas(7)
+    assert L.gemms_set_gemm_ctas(prev) == 7
