@@ -101,7 +101,7 @@ def test_pack_back_round_trip():
         assert err <= 2 ** -11, (r, err)
 
 
-def _leaver_worker(rank, world, port, outdir):
+def _leaver_worker(rank, world, port, outdir, combine="nccl", leave="before_layer"):
     import sys
     import time
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -110,27 +110,43 @@ def _leaver_worker(rank, world, port, outdir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
-    if rank == 1:
+    if rank == 1 and leave == "before_layer":
         return  # leaves between steps: never joins the layer's collectives
     d = _inputs()
     T, El = SHAPE.T // world, SHAPE.E // world
-    K = CpuEpKernels(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
+
+    class Leaving(CpuEpKernels):
+        def pack_back(self, rows, out=None):
+            # rank 1 leaves after the dispatch, before its rows go back
+            if rank == 1:
+                os._exit(0)
+            return super().pack_back(rows, out)
+
+    K = (Leaving if leave == "before_combine" else CpuEpKernels)(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
+    sl, el = slice(rank * T, (rank + 1) * T), slice(rank * El, (rank + 1) * El)
     t0 = time.time()
     status = "no-error"
     try:
-        EP.moe_ep(d["x"][:T], d["router_w"], d["router_bias"], d["w13"][:El], d["w13_scale"][:El], d["w2"][:El],
-                  d["w2_scale"][:El], n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k,
-                  routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K)
+        EP.moe_ep(d["x"][sl], d["router_w"], d["router_bias"], d["w13"][el], d["w13_scale"][el], d["w2"][el],
+                  d["w2_scale"][el], n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k,
+                  routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K, combine=combine)
     except RuntimeError as e:  # gloo: timeout or connection closed by the departed peer
         status = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
-    with open(os.path.join(outdir, "status.txt"), "w") as f:
-        f.write(status)
+    if rank == 0:
+        with open(os.path.join(outdir, "status.txt"), "w") as f:
+            f.write(status)
 
 
-def test_ep_rank_that_never_joins_is_detected():
+@pytest.mark.parametrize("combine,leave", [("nccl", "before_layer"), ("nccl", "before_combine"),
+                                           ("peer", "before_combine")])
+def test_ep_rank_that_leaves_is_detected(combine, leave):
+    """A rank that is gone (before the layer, or after the dispatch and before
+    its rows go back) makes the other rank's next collective (the count
+    exchange, the combine all-to-all, or the peer mode's barrier) fail within
+    the process group's timeout instead of waiting for ever."""
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_leaver_worker, args=(world, _free_port(), tmp), nprocs=world, join=True)
+        mp.spawn(_leaver_worker, args=(world, _free_port(), tmp, combine, leave), nprocs=world, join=True)
         status = open(os.path.join(tmp, "status.txt")).read()
     assert status.startswith("error after"), status
     secs = float(status.split()[2].rstrip("s:"))
