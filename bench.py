@@ -397,12 +397,12 @@ def gpu_arm(a):
                           **{k: v for k, v in kw.items() if k != "ep_group"})
             marks.append(tl)
         barrier()
-        recv_rows = [v for n, v in marks[0] if n == "recv_rows"][0]
-        marks = [[(n, e) for n, e in tl if n != "recv_rows"] for tl in marks]
+        info = {n: v for n, v in marks[0] if n in ("recv_rows", "pair_rows", "experts_hit")}
+        marks = [[(n, e) for n, e in tl if n not in info] for tl in marks]
         names = [n for n, _ in marks[0]]
         ep_timeline = {names[j]: round(statistics.median(tl[j - 1][1].elapsed_time(tl[j][1]) for tl in marks), 4)
                        for j in range(1, len(names))}
-        ep_timeline["recv_rows"] = recv_rows
+        ep_timeline.update(info)
     g1_ms = statistics.mean(evs[i][0].elapsed_time(evs[i][1]) for i in range(nev)) if nev else None
     g2_ms = statistics.mean(evs[i][1].elapsed_time(evs[i][2]) for i in range(nev)) if nev else None
     if group is None:
@@ -467,9 +467,17 @@ def gpu_arm(a):
     if group is not None:
         # Dominant phase at N>1: the grouped GEMMs over the received rows
         # (GEMM1 + GEMM2 of the rank's E/N experts, all of them hit at c3).
-        R = ep_timeline["recv_rows"]
-        ffn_bytes = (n_local * 3 * sh.I * sh.H + R * sh.H + 2 * R * planes * 2 * sh.I + 4 * R * sh.H
-                     + (3 * sh.I * sh.H + sh.T * sh.H if sh.shared else 0))
+        # same model as algorithmic_bytes: weights (+ scales) of the local
+        # experts hit (+ shared), the grouped rows (one per received row and
+        # local expert), the intermediate written and read, the fp32 result
+        # rows (received rows; the shared expert's T rows) read and written
+        H, I = sh.H, sh.I
+        w_exp = 3 * I * H + 4 * (2 * I // 128) * (H // 128) + 4 * (H // 128) * (I // 128)
+        row_b = H + 4 * H // 128
+        inter_b = 2 * (planes * I + 4 * I // 128)
+        R, P = ep_timeline["recv_rows"], ep_timeline["pair_rows"]
+        ffn_bytes = (ep_timeline["experts_hit"] * w_exp + P * (row_b + inter_b) + R * H * 4 * 2
+                     + ((w_exp + sh.T * (row_b + inter_b) + sh.T * H * 4 * 2) if sh.shared else 0))
         ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) + ep_timeline.get("shared_ffn_2", 0.0)
                                               if sh.shared else 0.0)
         ach = ffn_bytes / (ffn_ms / 1e3) / 1e9

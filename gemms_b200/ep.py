@@ -298,6 +298,19 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     mark("shared_ffn")
     work.wait()
     mark("dispatch_wait")
+    stats = None
+    if timeline is not None and R > 0:
+        # grouped-GEMM rows (one per received row and local expert it names)
+        # and local experts hit, for a roofline byte count; counted on the
+        # device now, read on the host after the last mark
+        off = H + 4 * (H // BLOCK)
+        ids = recv_buf[:R, off:off + 4 * top_k].contiguous().view(torch.int32)
+        le = ids.to(torch.int64) - rank * E_local
+        valid = (ids >= 0) & (le >= 0) & (le < E_local)
+        slot = torch.where(valid, le, torch.full_like(le, E_local)).flatten()  # no host sync (unlike masks)
+        per_expert = torch.zeros(E_local + 1, dtype=torch.int64, device=ids.device)
+        per_expert.scatter_add_(0, slot, torch.ones_like(slot))
+        stats = (valid.sum(), per_expert[:E_local])
 
     out_rows = K.expert_ffn(recv_buf, R, H, I, top_k, E_local, rank * E_local, inter_planes,
                             w13, w13_scale, w2, w2_scale)
@@ -313,6 +326,7 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
         mark("publish")
         out = K.combine_rows(acc, peers, row_add, send_row_of, world)
         mark("gather")
+        _timeline_stats(timeline, stats)
         return out
     packed = K.pack_back(out_rows)
     mark("pack_back")
@@ -326,4 +340,13 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     mark("combine_a2a")
     out = K.combine(acc, back, send_row_of, world)
     mark("gather")
+    _timeline_stats(timeline, stats)
     return out
+
+
+def _timeline_stats(timeline, stats):
+    if timeline is None:
+        return
+    pairs, per_expert = (0, None) if stats is None else (int(stats[0]), stats[1])
+    timeline.append(("pair_rows", pairs))
+    timeline.append(("experts_hit", 0 if per_expert is None else int((per_expert > 0).sum())))
