@@ -12,15 +12,20 @@ expert are replicated.  One layer forward on every rank:
    groups align with ranks, e.g. EP8 of DeepSeek-V3), rows grouped by
    destination in token order, quantised per 1x128 and packed with the ids and
    weights of the experts on the destination;
-3. count exchange (``all_to_all_single`` of int32, then one host read of the
-   split sizes) and the dispatch ``all_to_all_single`` of packed rows -- the
-   shared expert runs on the first half of the rank's own tokens meanwhile;
+3. count exchange (``all_gather`` of each rank's per-destination row counts,
+   then one host read of the count matrix) and the dispatch
+   ``all_to_all_single`` of packed rows -- the shared expert runs on the first
+   half of the rank's own tokens meanwhile (all of them with the peer
+   combine);
 4. grouped GEMMs over the received rows, each row's result pre-reduced over its
    local experts in fp32;
 5. the rows go back as fp16 with a per-row power-of-two scale (exact
    scaling, half the bytes of fp32), ``all_to_all_single`` while the shared
    expert runs on the second half of the tokens, and a deterministic
-   gather-sum per token plus the shared expert, cast to bf16.
+   gather-sum per token plus the shared expert, cast to bf16.  With the peer
+   combine (``combine="peer"``) the packed rows instead stay in a symmetric
+   buffer on the rank that computed them and, after one barrier, the gather
+   reads them from there over NVLink.
 
 Every rank issues the same collectives in the same order.  The device work
 goes through a ``kernels`` object: :class:`CudaEpKernels` (the C ABI) by
@@ -238,7 +243,9 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     ``w13``/``w2`` (and scales) hold this rank's ``E/W`` experts; the rank's
     first global expert is ``rank * E/W``.  ``timeline`` (a list) receives
     ``(phase, torch.cuda.Event)`` pairs recorded on the current stream at the
-    phase boundaries, for per-phase device timing.
+    phase boundaries, for per-phase device timing, and the counts
+    ``("recv_rows", R)``, ``("pair_rows", P)`` (grouped-GEMM rows: received
+    rows times the local experts each names) and ``("experts_hit", n)``.
 
     ``combine`` (default: ``GEMMS_EP_COMBINE``, else ``"nccl"``) picks how the
     result rows come back: ``"nccl"`` sends them with ``all_to_all_single``;
