@@ -11,14 +11,15 @@ combine + shared expert -> bf16) over one batch of synthetic tokens.
   top-4 groups / top-8, scaling 2.5, + 1 shared expert.  Inputs are resident in
   HBM; every step streams 11.3 GB of expert weights, far larger than the 126 MB
   L2, so no flush is needed between steps.
-* N>1 (torchrun): expert parallel over N ranks with the per-rank work of c1
-  held fixed -- 4096 tokens and E/N experts per rank, T = 4096*N in total, NCCL
-  all-to-all -- so value(N) / (N * value(1)) is a weak-scaling efficiency.  At
-  N=8 this is exactly BASELINE config c3 (T=32768, 32 experts per GPU).
+* N>1 (torchrun): BASELINE config c3 -- expert parallel over N ranks, T=32768
+  tokens in total (32768/N per rank), E/N experts per rank, NCCL all-to-all
+  dispatch/combine.  Total work is fixed as N grows ("strong" scaling).
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
 implementation of the path (the oracle restatement in ``oracle/``, bit-identical
-to ``flashinfer_baseline.run``) on the host cores instead.
+to ``flashinfer_baseline.run``) on the host cores instead, on the same inputs
+(drawn through the same generator path on GPU 0 and copied to the host) and
+with the same ``config`` dict as the GPU arm.
 """
 from __future__ import annotations
 
@@ -217,48 +218,143 @@ def cpu_baseline(sh, d_dev, logits_dev, n_experts_sample: int, threads: int | No
             "os_cpu_count": os.cpu_count()}
 
 
-def reference_arm(a, sh):
-    """--impl reference: the reference's CPU path (oracle port) on host cores.
-    One step = one call of the reference's run() over all T tokens with
-    E_local=8 local experts (1/32 of the routed experts; the reference's own
-    calls use E_local=32, so each step charges the per-call activation dequant
-    and routing 4x more often than the reference would -- a conservative,
-    slightly slow figure for the CPU).  Throughput scales by (E+1)/8 units."""
+def bench_setup(a, world: int, rank: int, dev):
+    """Config and seeded inputs of this rank, shared by both arms.  Returns
+    (cfg name, base shape, per-rank shape, local expert count, inputs on dev,
+    Zipf histogram or None)."""
     import torch
 
+    import gemms_b200
     from gemms_b200 import workloads as W
+
+    cfg = a.config or ("c1" if world == 1 else "c3")
+    base = parse_config(cfg)
+    T_rank = base.T // world if world > 1 else base.T
+    sh = base.replace(T=T_rank)
+    n_local = sh.E // world
+    zipf_hist = None
+    d = W.make_inputs(sh, seed=rank, device=dev, experts=n_local)
+    # every rank must hold the same router weights/bias and shared expert
+    g = torch.Generator(device=dev).manual_seed(12345)
+    d["router_w"] = torch.randn((sh.E, sh.H), generator=g, device=dev) * 0.02
+    d["router_bias"] = torch.rand((sh.E,), generator=g, device=dev) * 0.2 - 0.1
+    if sh.shared:
+        d["shared_w13"] = torch.randn((2 * sh.I, sh.H), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
+        d["shared_w13_scale"] = torch.rand((2 * sh.I // 128, sh.H // 128), generator=g, device=dev) * 2e-3 + 1e-3
+        d["shared_w2"] = torch.randn((sh.H, sh.I), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
+        d["shared_w2_scale"] = torch.rand((sh.H // 128, sh.I // 128), generator=g, device=dev) * 2e-3 + 1e-3
+    if cfg.startswith("c4"):
+        # BASELINE c4: router bias calibrated so expert popularity follows
+        # Zipf(1.2) over a seeded permutation, hottest experts on ranks 0-1.
+        route_fn = lambda lg, b: gemms_b200.route(lg, b, n_group=sh.n_group, topk_group=sh.topk_group,
+                                                  top_k=sh.top_k, routed_scaling_factor=sh.rsf, counts=False)[0]
+        bias, frac = W.zipf_bias(sh, route_fn, router_w=d["router_w"], s=1.2, seed=0, hot_ranks=2, world=8,
+                                 device=dev)
+        d["router_bias"] = bias
+        zipf_hist = frac.cpu()
+    return cfg, base, sh, n_local, d, zipf_hist
+
+
+def config_dict(cfg, base, sh, n_local, planes, world, zipf_hist=None):
+    c = {"workload": (f"{cfg}: DeepSeek-V3 MoE layer T={base.T} H={sh.H} I={sh.I} E={sh.E} "
+                      f"groups {sh.n_group}/{sh.topk_group} top-{sh.top_k}" + (" + shared expert" if sh.shared else "")),
+         "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
+         "parallelism": f"ep{world}" if world > 1 else "single GPU",
+         **({"ep_combine": os.environ.get("GEMMS_EP_COMBINE", "nccl")} if world > 1 else {}),
+         "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"}
+    if zipf_hist is not None:
+        per_rank = zipf_hist.reshape(8, -1).sum(1)
+        c["zipf"] = {"s": 1.2, "top_expert_share": float(zipf_hist.max()),
+                     "rank_share_of_routed_pairs": [round(float(v), 4) for v in per_rank]}
+    return c
+
+
+REF_E_LOCAL = 32     # the reference's own E_local (flashinfer_baseline.py:45)
+REF_TOKENS = 4096    # tokens per reference call (one rank's c1 batch)
+
+
+def reference_arm(a):
+    """--impl reference: the reference's CPU path (the oracle port, bit-identical
+    to flashinfer_baseline.run) on the host cores, on the GPU arm's inputs and
+    config.  One step = one reference run() call over up to 4096 of rank 0's
+    tokens with E_local=32 local experts, as the reference calls it; the
+    layer's throughput is that call's time scaled to all tokens and all E
+    experts, plus the shared expert (timed once on the same tokens)."""
+    import torch
+
     from oracle import reference_moe as R
 
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    per_step = 8
-    d = W.make_inputs(sh, seed=0, experts=per_step)
-    logits = R.router_logits(d["x"], d["router_w"])
-    hs, hss = R.quantize_1x128(d["x"])
-    # Make expert 0 receive its typical share: route with the real logits.
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    planes = 2
+    cfg, base, sh, n_local, d, zipf_hist = bench_setup(a, world, 0, dev)
+    ts = min(sh.T, REF_TOKENS)
+    el = min(REF_E_LOCAL, n_local)
+    x = d["x"][:ts].cpu()
+    cw = {k: d[k][:el].cpu() for k in ("w13", "w13_scale", "w2", "w2_scale")}
+    router_w, bias = d["router_w"].cpu(), d["router_bias"].cpu()
+    shared = [d[k].cpu() for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale")] \
+        if sh.shared else None
+    del d
+    torch.cuda.empty_cache()
+    logits = R.router_logits(x, router_w)
+    hs, hss = R.quantize_1x128(x)
     times = []
     for i in range(a.warmup + a.steps):
         t0 = time.perf_counter()
-        R.run_local(logits, d["router_bias"], hs, hss, d["w13"], d["w13_scale"], d["w2"], d["w2_scale"], 0,
-                    sh.rsf, n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, return_fp32=True)
+        R.run_local(logits, bias, hs, hss, cw["w13"], cw["w13_scale"], cw["w2"], cw["w2_scale"], 0, sh.rsf,
+                    n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, return_fp32=True)
         dt = time.perf_counter() - t0
         if i >= a.warmup:
             times.append(dt)
-    units = (sh.E + (1 if sh.shared else 0)) / per_step
-    ms = statistics.mean(times) * 1e3
-    value = (sh.T / units) / (ms / 1e3)
+    t_shared = 0.0
+    if shared is not None:
+        A = R.dequant_hidden(hs, hss)
+        t0 = time.perf_counter()
+        R.shared_expert(A, *shared)
+        t_shared = time.perf_counter() - t0
+    t_call = statistics.mean(times)
+    token_scale = base.T / ts
+    t_layer = t_call * token_scale * (sh.E / el) + t_shared * token_scale
+    value = base.T / t_layer
     cores = torch.get_num_threads()
-    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": a.gpus,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (fp8 dequantised)", "data": "synthetic (seeded, BASELINE c1 shapes)",
-            "config": {"workload": "c1: DeepSeek-V3 MoE layer T=4096 H=7168 I=2048 E=256 top-8 + shared expert",
-                       "step": "one reference run() call: all 4096 tokens, E_local=8 of 256 routed experts"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": "per step: oracle port of flashinfer_baseline.run (bit-identical) over "
-                                       "T=4096 tokens for 8 of 257 expert units of the c1 layer, scaled by 257/8"},
+    sample = (f"per step: one oracle run() call (== reference flashinfer_baseline.run) over {ts} of rank 0's "
+              f"tokens with E_local={el} local experts ({t_call:.2f} s); layer = call x {token_scale:g} token "
+              f"slices x {sh.E // el} expert slices + shared expert ({t_shared:.2f} s per slice) = {t_layer:.1f} s")
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": t_call * 1e3, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (fp8 dequantised)",
+            "data": "synthetic (seeded; BASELINE distributions; random-init weights)",
+            "config": config_dict(cfg, base, sh, n_local, planes, world, zipf_hist),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
+                             "os_cpu_count": os.cpu_count()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def fp8_peak_tflops(dev, n: int = 8192, reps: int = 10):
+    """Dense FP8 tensor peak of this GPU measured with a library GEMM:
+    torch._scaled_mm (cuBLAS) on e4m3 n x n x n, bf16 out, best of `reps`."""
+    import torch
+
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+    for _ in range(3):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
 
 
 # --------------------------------------------------------------- GPU arm
@@ -295,34 +391,8 @@ def gpu_arm(a):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
-    cfg = a.config or ("c1" if world == 1 else f"c3:T={4096 * world}")
-    base = parse_config(cfg)
-    T_rank = base.T // world if world > 1 else base.T
-    sh = base.replace(T=T_rank)
     planes = 2
-
-    # inputs: this rank's tokens; this rank's E/world experts (EP) or all E
-    n_local = sh.E // world
-    zipf_hist = None
-    d = W.make_inputs(sh, seed=rank, device=dev, experts=n_local)
-    # every rank must hold the same router weights/bias and shared expert
-    g = torch.Generator(device=dev).manual_seed(12345)
-    d["router_w"] = torch.randn((sh.E, sh.H), generator=g, device=dev) * 0.02
-    d["router_bias"] = torch.rand((sh.E,), generator=g, device=dev) * 0.2 - 0.1
-    if sh.shared:
-        d["shared_w13"] = torch.randn((2 * sh.I, sh.H), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
-        d["shared_w13_scale"] = torch.rand((2 * sh.I // 128, sh.H // 128), generator=g, device=dev) * 2e-3 + 1e-3
-        d["shared_w2"] = torch.randn((sh.H, sh.I), generator=g, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn)
-        d["shared_w2_scale"] = torch.rand((sh.H // 128, sh.I // 128), generator=g, device=dev) * 2e-3 + 1e-3
-    if cfg.startswith("c4"):
-        # BASELINE c4: router bias calibrated so expert popularity follows
-        # Zipf(1.2) over a seeded permutation, hottest experts on ranks 0-1.
-        route_fn = lambda lg, b: gemms_b200.route(lg, b, n_group=sh.n_group, topk_group=sh.topk_group,
-                                                  top_k=sh.top_k, routed_scaling_factor=sh.rsf, counts=False)[0]
-        bias, frac = W.zipf_bias(sh, route_fn, router_w=d["router_w"], s=1.2, seed=0, hot_ranks=2, world=8,
-                                 device=dev)
-        d["router_bias"] = bias
-        zipf_hist = frac.cpu()
+    cfg, base, sh, n_local, d, zipf_hist = bench_setup(a, world, rank, dev)
     shared_kw = {k: d[k] for k in ("shared_w13", "shared_w13_scale", "shared_w2", "shared_w2_scale") if k in d}
     kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
               inter_planes=planes, ep_group=group, **shared_kw)
@@ -446,24 +516,20 @@ def gpu_arm(a):
             dist.destroy_process_group()
         return
     hbm, bf16, src = _peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    fp8_peak = fp8_peak_tflops(dev)
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)",
             "data": "synthetic (seeded; BASELINE distributions; random-init weights)",
-            "config": {"workload": (f"{cfg}: DeepSeek-V3 MoE layer T={base.T} H={sh.H} I={sh.I} E={sh.E} "
-                                    f"groups {sh.n_group}/{sh.topk_group} top-{sh.top_k}"
-                                    + (" + shared expert" if sh.shared else "")),
-                       "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
-                       "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                       **({"ep_combine": os.environ.get("GEMMS_EP_COMBINE", "nccl")} if world > 1 else {}),
-                       "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"},
-            "tflops": flops / (ms / 1e3) / 1e12,
+            "config": config_dict(cfg, base, sh, n_local, planes, world, zipf_hist),
+            "tflops": tflops,
+            "fp8": {"tflops": tflops, "peak_tflops": fp8_peak, "frac": tflops / fp8_peak,
+                    "peak_source": "measured in this run: torch._scaled_mm (cuBLAS) e4m3 8192^3, bf16 out, "
+                                   "best of 10 on this GPU"},
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
             "e2e": e2e, "clocks": clocks}
-    if zipf_hist is not None:
-        per_rank = zipf_hist.reshape(8, -1).sum(1)
-        line["config"]["zipf"] = {"s": 1.2, "top_expert_share": float(zipf_hist.max()),
-                                  "rank_share_of_routed_pairs": [round(float(v), 4) for v in per_rank]}
     if group is not None:
         # Dominant phase at N>1: the grouped GEMMs over the received rows
         # (GEMM1 + GEMM2 of the rank's E/N experts, all of them hit at c3).
@@ -514,13 +580,7 @@ def gpu_arm(a):
 def main():
     a = _args()
     if a.impl == "reference":
-        from gemms_b200 import workloads as W
-
-        world = int(os.environ.get("WORLD_SIZE", "1"))
-        sh = W.CONFIGS["c1"]
-        if world > 1 and int(os.environ.get("RANK", "0")) != 0:
-            return
-        reference_arm(a, sh)
+        reference_arm(a)
         return
     gpu_arm(a)
 

@@ -7,13 +7,15 @@ Public operators (CUDA tensors only, no CPU fallback):
 * :func:`moe` -- the full layer ``moe(x, router_w, router_bias, w13, w13_scale,
   w2, w2_scale, ...)``, optionally expert-parallel over a process group.
 * :func:`route` -- the group-limited sigmoid top-k router alone.
+* :func:`router_logits`, :func:`quantize_1x128` -- the router GEMM and the
+  per-1x128 activation quantisation alone.
 * :class:`MoePipeline` -- host-to-host serving loop with PCIe copies overlapped.
 """
-from .ops import ShapeError, check_device_errors, moe, route, router_logits, run  # noqa: F401
+from .ops import ShapeError, check_device_errors, moe, quantize_1x128, route, router_logits, run  # noqa: F401
 from ._lib import GemmsError, lib_path, load as load_library  # noqa: F401
 from . import workloads  # noqa: F401
 from .pipeline import MoePipeline  # noqa: F401
 
-__all__ = ["run", "moe", "route", "router_logits", "ShapeError", "GemmsError", "check_device_errors",
+__all__ = ["run", "moe", "route", "router_logits", "quantize_1x128", "ShapeError", "GemmsError", "check_device_errors",
            "load_library", "lib_path", "workloads", "MoePipeline"]
 __version__ = "0.1.0"

@@ -38,6 +38,12 @@ EXPORTS = (
     "gemms_ep_combine",
     "gemms_ep_combine_rows",
     "gemms_set_gemm_ctas",
+    "gemms_moe_fwd_noalloc",
+    "gemms_moe_check_noalloc",
+    "gemms_test_inject_stall",
+    "gemms_router_workspace_size",
+    "gemms_router_logits",
+    "gemms_quantize_1x128",
 )
 
 
@@ -59,16 +65,29 @@ class GemmsMoeArgs(ctypes.Structure):
         ("shared_w13", c_void_p), ("shared_w13_scale", c_void_p), ("shared_w2", c_void_p),
         ("shared_w2_scale", c_void_p),
         ("out", c_void_p), ("topk_idx_out", c_void_p), ("topk_w_out", c_void_p), ("expert_counts_out", c_void_p),
-        ("profile_events", c_void_p),
+        ("profile_events", c_void_p), ("router_w", c_void_p), ("logits_out", c_void_p),
     ]
 
 
-class GemmsError(RuntimeError):
-    """A GEMMS_ERR_* code returned by the C ABI."""
+GEMMS_ERR_TIMEOUT = -5
 
-    def __init__(self, code: int, where: str):
+# Bits of the device error word (GEMMS_FLAG_* in include/gemms_moe.h).
+FLAG_PRODUCER_WAIT = 1 << 0
+FLAG_MMA_WAIT = 1 << 1
+FLAG_EPILOGUE_WAIT = 1 << 2
+FLAG_BAD_EXPERT = 1 << 3
+FLAG_ROW_OVERFLOW = 1 << 4
+
+
+class GemmsError(RuntimeError):
+    """A GEMMS_ERR_* code returned by the C ABI (``flags``: the device error
+    word's bits when the code came from a device-side check)."""
+
+    def __init__(self, code: int, where: str, flags: int = 0):
         self.code = code
-        super().__init__(f"{where} failed: {strerror(code)} (code {code})")
+        self.flags = flags
+        extra = f", device error word 0x{flags:x}" if flags else ""
+        super().__init__(f"{where} failed: {strerror(code)} (code {code}{extra})")
 
 
 _lib = None
@@ -134,6 +153,19 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
                                             c_void_p, c_void_p]
         L.gemms_ep_combine_rows.restype = c_int32
         L.gemms_ep_combine.restype = c_int32
+        L.gemms_moe_fwd_noalloc.argtypes = [ctypes.POINTER(GemmsMoeArgs), c_void_p]
+        L.gemms_moe_fwd_noalloc.restype = c_int32
+        L.gemms_moe_check_noalloc.argtypes = [c_void_p, ctypes.POINTER(c_int32)]
+        L.gemms_moe_check_noalloc.restype = c_int32
+        L.gemms_test_inject_stall.argtypes = [c_int32, c_int32, ctypes.c_int64]
+        L.gemms_test_inject_stall.restype = c_int32
+        L.gemms_router_workspace_size.argtypes = [c_int32, c_int32, c_int32]
+        L.gemms_router_workspace_size.restype = c_size_t
+        L.gemms_router_logits.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                          c_size_t, c_void_p]
+        L.gemms_router_logits.restype = c_int32
+        L.gemms_quantize_1x128.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]
+        L.gemms_quantize_1x128.restype = c_int32
         _lib = L
         return L
 

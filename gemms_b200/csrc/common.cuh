@@ -6,6 +6,8 @@
 #include <cstdint>
 #include <cstddef>
 
+#include <cudaTypedefs.h>
+
 #include "gemms_moe.h"
 
 namespace gemms {
@@ -15,11 +17,11 @@ constexpr float kFp8Max = 448.0f;    // largest finite e4m3 magnitude
 
 // Device error word bits (OR-ed by kernels, read by gemms_moe_check).
 enum : int {
-  kErrGemmProducerWait = 1 << 0,
-  kErrGemmMmaWait = 1 << 1,
-  kErrGemmEpilogueWait = 1 << 2,
-  kErrBadExpertIndex = 1 << 3,
-  kErrRowOverflow = 1 << 4,
+  kErrGemmProducerWait = GEMMS_FLAG_PRODUCER_WAIT,
+  kErrGemmMmaWait = GEMMS_FLAG_MMA_WAIT,
+  kErrGemmEpilogueWait = GEMMS_FLAG_EPILOGUE_WAIT,
+  kErrBadExpertIndex = GEMMS_FLAG_BAD_EXPERT,
+  kErrRowOverflow = GEMMS_FLAG_ROW_OVERFLOW,
 };
 
 #define GEMMS_CUDA_TRY(expr)                         \
@@ -35,7 +37,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // ---- internal launchers (stream-ordered, return GEMMS_* codes) ----------
 struct RouteArgs {
-  const float* logits;
+  const float* logits;        // fp32 [T, E], or nullptr when `partials` is given
+  const float* partials;      // fp32 [n_partials][T][E] router-GEMM split-K partials, summed in order
+  int n_partials;
+  float* logits_out;          // optional fp32 [T, E]: the summed logits (partials path only)
   const void* bias;
   int bias_bf16;
   int T, E, n_group, topk_group, top_k;
@@ -97,6 +102,9 @@ struct PermuteArgs {
 };
 int launch_permute(const PermuteArgs& a, cudaStream_t s);
 
+// Token-major per-1x128 quantisation: bf16 [T, H] -> e4m3 [T, H] + fp32 scale [H/128, T].
+int launch_quantize(const __nv_bfloat16* x, int T, int H, uint8_t* xq, float* xq_scale, cudaStream_t s);
+
 // fp32 [n] -> bf16 [n]
 int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s);
 
@@ -133,6 +141,31 @@ struct Gemm2Args {
   int* err;
 };
 int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
+
+// Router GEMM (router_gemm.cu): logits = x . router_w^T via a bf16 hi/lo split.
+struct RouterPlan {
+  int Np;            // E rounded up to 16 (MMA N)
+  int KB;            // 64-element K blocks
+  int kb_per_split;
+  int splits;        // split-K factor (partials summed by route_kernel / launch_sum_partials)
+  size_t split_bytes;    // bf16 planes [2][Np][H]
+  size_t partial_bytes;  // fp32 [splits][T][E]
+};
+RouterPlan router_plan(int T, int H, int E);
+struct RouterGemmArgs {
+  RouterPlan plan;
+  const __nv_bfloat16* x;  // [T, H]
+  const float* router_w;   // [E, H]
+  int T, H, E;
+  __nv_bfloat16* planes;   // workspace, plan.split_bytes
+  float* partials;         // workspace, plan.partial_bytes
+  int* err;
+};
+int launch_router_gemm(const RouterGemmArgs& a, cudaStream_t s);
+int launch_sum_partials(const float* partials, int splits, int T, int E, float* logits, cudaStream_t s);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 
 int num_sms();
 int gemm_ctas();  // persistent GEMM grid bound (gemms_set_gemm_ctas)

@@ -103,6 +103,13 @@ struct GemmParams {
   float* out;
   int H;
   int* err;
+  // Bounded waits: cycles before a pipeline wait gives up (product default
+  // GEMMS_WAIT_TIMEOUT_CYCLES).  stall_iter >= 0 is a test hook: CTA 0's
+  // producer stops issuing at that K iteration (nothing left in flight), so
+  // the MMA thread's wait for the missing stage runs out and reports
+  // kErrGemmMmaWait through the error word.
+  long long wait_limit;
+  int stall_iter;
 };
 
 __device__ __forceinline__ uint16_t f2_to_e4m3x2(float a, float b) {
@@ -217,7 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_l2_2d(pmb, pkb * BK, pwrow, pol_w);
             tma_prefetch_l2_2d(pmb, pkb * BK, pwrow + p.b_row_hi, pol_w);
           }
-          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+          if (blockIdx.x == 0 && it == p.stall_iter) {
+            ok = false;  // test hook: withhold this stage (no expect_tx, no loads)
+            break;
+          }
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait, p.wait_limit)) {
             ok = false;
             break;
           }
@@ -264,11 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // released, so its (cheap, satisfied) wait goes first and the
           // buffer wait is the last step before the MMAs.
           const int s = it % S;
-          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, p.err, kErrGemmMmaWait, p.wait_limit)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait,
+                         p.wait_limit)) {
             ok = false;
             break;
           }
@@ -358,7 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = acc_it & 1;
         // One lane polls the barrier; the warp waits at __syncwarp.
         int got = 1;
-        if (lane == 0) got = mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait);
+        if (lane == 0)
+          got = mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait, p.wait_limit);
         got = __shfl_sync(0xffffffffu, got, 0);
         __syncwarp();
         if (!got) {
@@ -489,6 +502,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
+// Test hook state (gemms_test_inject_stall): which GEMM (1 or 2, 0 = none)
+// stalls at which K iteration, and the pipeline wait limit in SM cycles.
+std::atomic<int> g_stall_gemm{0};
+std::atomic<int> g_stall_iter{-1};
+std::atomic<long long> g_wait_limit{GEMMS_WAIT_TIMEOUT_CYCLES};
+
+void apply_wait_knobs(GemmParams& p, int gemm) {
+  p.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  p.stall_iter = g_stall_gemm.load(std::memory_order_relaxed) == gemm ? g_stall_iter.load(std::memory_order_relaxed)
+                                                                        : -1;
+}
+
 // Weight K-blocks a CTA keeps in flight toward L2 beyond its smem ring.  The
 // weight stream is DRAM-latency bound (one 32 KB stage per K-block per SM);
 // GEMMS_PREFETCH overrides the default for tuning.
@@ -501,19 +526,6 @@ int prefetch_depth() {
     if (depth > 64) depth = 64;
   }
   return depth;
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
 }
 
 // 2-D uint8 tensor [rows, inner] with a 128x128 box and 128-byte swizzle.
@@ -554,6 +566,19 @@ int launch_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
 int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   if (a.H % BK || a.I % BK) return GEMMS_ERR_SHAPE;
   if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
@@ -590,6 +615,7 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.I = a.I;
   p.H = a.H;
   p.err = a.err;
+  apply_wait_knobs(p, 1);
   const int max_units = a.g.max_tiles * p.n_tiles;
   if (a.planes == 2) return launch_kernel<0, 1, 2>(ma, mb, mbs, p, max_units, s);
   return launch_kernel<0, 1, 3>(ma, mb, mbs, p, max_units, s);
@@ -631,6 +657,7 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.H = a.H;
   p.I = a.I;
   p.err = a.err;
+  apply_wait_knobs(p, 2);
   const int max_units = a.g.max_tiles * p.n_tiles;
   if (a.planes == 2) return launch_kernel<1, 2, 1>(ma, mb, mbs, p, max_units, s);
   return launch_kernel<1, 3, 1>(ma, mb, mbs, p, max_units, s);
@@ -660,6 +687,21 @@ int num_sms() {
 }
 
 }  // namespace gemms
+
+extern "C" int gemms_test_inject_stall(int32_t gemm, int32_t k_iteration, int64_t wait_limit_cycles) {
+  if (gemm < 0 || gemm > 2 || wait_limit_cycles < 0) return GEMMS_ERR_ARG;
+  if (gemm == 0) {
+    gemms::g_stall_gemm.store(0);
+    gemms::g_stall_iter.store(-1);
+    gemms::g_wait_limit.store(GEMMS_WAIT_TIMEOUT_CYCLES);
+    return GEMMS_OK;
+  }
+  if (k_iteration < 0) return GEMMS_ERR_ARG;
+  gemms::g_wait_limit.store(wait_limit_cycles > 0 ? wait_limit_cycles : GEMMS_WAIT_TIMEOUT_CYCLES);
+  gemms::g_stall_iter.store(k_iteration);
+  gemms::g_stall_gemm.store(gemm);
+  return GEMMS_OK;
+}
 
 extern "C" int gemms_set_gemm_ctas(int32_t max_ctas) {
   if (max_ctas < 0) return GEMMS_ERR_ARG;

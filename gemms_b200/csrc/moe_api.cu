@@ -17,6 +17,8 @@ struct FwdLayout {
   int R_max, groups, max_tiles, scale_ld;
   size_t err, counts, topk_idx, topk_w, pair_row, offsets, tile_group, tile_row0, tile_rows, num_tiles;
   size_t row_token, row_weight, a_rows, a_scale, inter, inter_scale, out_acc, total;
+  RouterPlan router;
+  size_t router_planes, router_partials;  // router GEMM scratch (GEMMS_INPUT_BF16 only)
   size_t head_bytes;  // [0, head_bytes) is zeroed each call (error word + counts)
 };
 
@@ -57,6 +59,11 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.inter = take((size_t)std::max(L.R_max, 1) * L.planes * L.I);
   L.inter_scale = take(sizeof(float) * (size_t)(L.I / kBlock) * L.scale_ld);
   L.out_acc = take(sizeof(float) * (size_t)L.T * L.H);
+  if (s.input_mode == GEMMS_INPUT_BF16) {
+    L.router = router_plan(s.T, s.H, s.E);
+    L.router_planes = take(L.router.split_bytes);
+    L.router_partials = take(L.router.partial_bytes);
+  }
   L.total = o;
   return L;
 }
@@ -132,7 +139,11 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   const FwdLayout L = fwd_layout(s);
   if (!workspace || ws_bytes < L.total) return GEMMS_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GEMMS_ERR_ALIGN;
-  if (!args->routing_logits || !args->routing_bias || !args->out) return GEMMS_ERR_ARG;
+  const bool gemm_router = args->routing_logits == nullptr;
+  if (!args->routing_bias || !args->out) return GEMMS_ERR_ARG;
+  if (gemm_router && (s.input_mode != GEMMS_INPUT_BF16 || !args->router_w || !args->hidden_bf16))
+    return GEMMS_ERR_ARG;
+  if (gemm_router && !aligned16(args->router_w)) return GEMMS_ERR_ALIGN;
   if (s.E_local > 0 && (!args->w13 || !args->w13_scale || !args->w2 || !args->w2_scale)) return GEMMS_ERR_ARG;
   if (s.input_mode == GEMMS_INPUT_BF16 && !args->hidden_bf16) return GEMMS_ERR_ARG;
   if (s.input_mode == GEMMS_INPUT_FP8 && (!args->hidden_fp8 || !args->hidden_scale)) return GEMMS_ERR_ARG;
@@ -150,7 +161,27 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
 
   RouteArgs ra{};
-  ra.logits = args->routing_logits;
+  if (gemm_router) {
+    RouterGemmArgs rg{};
+    rg.plan = L.router;
+    rg.x = static_cast<const __nv_bfloat16*>(args->hidden_bf16);
+    rg.router_w = args->router_w;
+    rg.T = s.T;
+    rg.H = s.H;
+    rg.E = s.E;
+    rg.planes = at<__nv_bfloat16>(ws, L.router_planes);
+    rg.partials = at<float>(ws, L.router_partials);
+    rg.err = err;
+    if ((rc = launch_router_gemm(rg, st))) return rc;
+    ra.partials = rg.partials;
+    ra.n_partials = L.router.splits;
+    ra.logits_out = args->logits_out;
+  } else {
+    ra.logits = args->routing_logits;
+    if (args->logits_out)
+      GEMMS_CUDA_TRY(cudaMemcpyAsync(args->logits_out, args->routing_logits, sizeof(float) * (size_t)s.T * s.E,
+                                     cudaMemcpyDeviceToDevice, st));
+  }
   ra.bias = args->routing_bias;
   ra.bias_bf16 = s.bias_bf16;
   ra.T = s.T;

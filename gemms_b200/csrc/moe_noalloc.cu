@@ -61,3 +61,15 @@ extern "C" int gemms_moe_fwd_noalloc(const GemmsMoeArgs* args, gemms_stream_t st
   // fully written before it is read.
   return gemms_moe_fwd(args, ws, kNoallocScratchBytes, stream);
 }
+
+// The error word of gemms_moe_fwd_noalloc lives in the same fixed array, so
+// its callers have no workspace pointer to hand to gemms_moe_check; this looks
+// the array up on the current device and reads (and clears) the word there.
+// Synchronises the stream, like gemms_moe_check.
+extern "C" int gemms_moe_check_noalloc(gemms_stream_t stream, int32_t* flags) {
+  if (!flags) return GEMMS_ERR_ARG;
+  void* ws = nullptr;
+  int rc = scratch_address(&ws);
+  if (rc) return rc;
+  return gemms_moe_check(ws, stream, flags);
+}

@@ -8,6 +8,8 @@
 // epilogue warp reads the scales of 32 consecutive rows as one coalesced load.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace gemms {
 namespace {
 
@@ -66,6 +68,51 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a) {
   }
 }
 
+// Token-major per-1x128 quantisation: x bf16 [T, H] -> xq e4m3 [T, H] and
+// xq_scale fp32 [H/128, T] (the reference's transposed hidden_states_scale
+// layout, flashinfer_baseline.py:59,72).  A thread owns 16 consecutive
+// columns (two 16-byte loads, one 16-byte store); the 8 threads of a
+// 128-column block exchange their amax with three shuffles.
+__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                       uint8_t* __restrict__ xq, float* __restrict__ xq_scale) {
+  const int per_row = H / 16;
+  const size_t total = (size_t)T * per_row;
+  // Whole warps iterate together (the shuffles below need all 32 lanes).
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i0 = (size_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31u); i0 < total; i0 += stride) {
+    const size_t i = i0 + (threadIdx.x & 31);
+    const bool live = i < total;
+    const size_t ii = live ? i : total - 1;
+    const int t = static_cast<int>(ii / per_row);
+    const int c16 = static_cast<int>(ii - (size_t)t * per_row);
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H + 16 * (size_t)c16);
+    const uint4 r0 = src[0], r1 = src[1];
+    float v[16];
+    const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
+      v[2 * k] = __low2float(b);
+      v[2 * k + 1] = __high2float(b);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(v[k]));
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+    uint4 q;
+    q.x = quant4(v[0], v[1], v[2], v[3], scale);
+    q.y = quant4(v[4], v[5], v[6], v[7], scale);
+    q.z = quant4(v[8], v[9], v[10], v[11], scale);
+    q.w = quant4(v[12], v[13], v[14], v[15], scale);
+    if (live) {
+      *reinterpret_cast<uint4*>(xq + (size_t)t * H + 16 * (size_t)c16) = q;
+      if ((c16 & 7) == 0) xq_scale[(size_t)(c16 >> 3) * T + t] = scale;
+    }
+  }
+}
+
 __global__ void to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, size_t n4) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     const float4 v = in[i];
@@ -88,6 +135,17 @@ int launch_permute(const PermuteArgs& a, cudaStream_t s) {
   return GEMMS_OK;
 }
 
+int launch_quantize(const __nv_bfloat16* x, int T, int H, uint8_t* xq, float* xq_scale, cudaStream_t s) {
+  if (T <= 0) return GEMMS_OK;
+  if (H % kBlock) return GEMMS_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(xq)) return GEMMS_ERR_ALIGN;
+  const size_t total = (size_t)T * (H / 16);
+  const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 16));
+  quantize_kernel<<<blocks, 256, 0, s>>>(x, T, H, xq, xq_scale);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
 int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s) {
   if (n == 0) return GEMMS_OK;
   if (n % 4) return GEMMS_ERR_SHAPE;
@@ -99,3 +157,12 @@ int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s
 }
 
 }  // namespace gemms
+
+extern "C" int gemms_quantize_1x128(const void* x_bf16, int32_t T, int32_t H, void* xq, float* xq_scale,
+                                    gemms_stream_t stream) {
+  if (T < 0 || H <= 0 || H % gemms::kBlock) return GEMMS_ERR_SHAPE;
+  if (T == 0) return GEMMS_OK;
+  if (!x_bf16 || !xq || !xq_scale) return GEMMS_ERR_ARG;
+  return gemms::launch_quantize(static_cast<const __nv_bfloat16*>(x_bf16), T, H, static_cast<uint8_t*>(xq), xq_scale,
+                                reinterpret_cast<cudaStream_t>(stream));
+}

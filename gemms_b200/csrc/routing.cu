@@ -7,6 +7,7 @@
 // attempt, which hard-codes group size 32, uses ex2.approx for the sigmoid
 // and assigns rows with atomics, i.e. in nondeterministic order).
 #include "common.cuh"
+#include <algorithm>
 #include <cfloat>
 
 namespace gemms {
@@ -52,7 +53,16 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
     sb[j] = -INFINITY;
     const int e = j * 32 + lane;
     if (j < V && e < E) {
-      const float x = __ldg(a.logits + (size_t)t * E + e);
+      float x;
+      if (a.partials) {
+        // router-GEMM split-K partials, summed in split order (deterministic)
+        const float* pp = a.partials + (size_t)t * E + e;
+        x = pp[0];
+        for (int q = 1; q < a.n_partials; ++q) x = __fadd_rn(x, pp[(size_t)q * a.T * E]);
+        if (a.logits_out) a.logits_out[(size_t)t * E + e] = x;
+      } else {
+        x = __ldg(a.logits + (size_t)t * E + e);
+      }
       const float ex = static_cast<float>(exp(-static_cast<double>(x)));
       s[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
       const float bias = a.bias_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[e])
@@ -261,7 +271,25 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
   }
 }
 
+// logits[t][e] = sum over q of partials[q][t][e], in split order (as route_kernel).
+__global__ void sum_partials_kernel(const float* __restrict__ partials, int splits, size_t n, float* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float x = partials[i];
+    for (int q = 1; q < splits; ++q) x = __fadd_rn(x, partials[(size_t)q * n + i]);
+    out[i] = x;
+  }
+}
+
 }  // namespace
+
+int launch_sum_partials(const float* partials, int splits, int T, int E, float* logits, cudaStream_t s) {
+  const size_t n = (size_t)T * E;
+  if (n == 0) return GEMMS_OK;
+  const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, (size_t)num_sms() * 8));
+  sum_partials_kernel<<<blocks, 256, 0, s>>>(partials, splits, n, logits);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
 
 int launch_route(const RouteArgs& a, cudaStream_t s) {
   if (a.T <= 0) return GEMMS_OK;

@@ -68,19 +68,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with `parity` to complete.  Returns false (after
-// setting *abort and OR-ing `code` into *err) when the wait exceeds the
-// timeout, or as soon as another role has raised *abort.  The timeout runs on
-// the SM cycle counter (cheap to read), checked every 256 polls; reading
-// %globaltimer on every miss added ~1 us to each pipeline hand-off.
+// setting *abort and OR-ing `code` into *err) when the wait exceeds
+// `limit_cycles`, or as soon as another role has raised *abort.  The timeout
+// runs on the SM cycle counter (cheap to read), checked every 256 polls;
+// reading %globaltimer on every miss added ~1 us to each pipeline hand-off.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+                                          int* err, int code, long long limit_cycles = GEMMS_WAIT_TIMEOUT_CYCLES) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++n & 255u) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > GEMMS_WAIT_TIMEOUT_CYCLES) {
+      if (clock64() - t0 > limit_cycles) {
         *abort_flag = 1;
         atomicOr(err, code);
         return false;

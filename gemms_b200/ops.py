@@ -113,7 +113,7 @@ def check_device_errors(ws: torch.Tensor | None = None, tag: str = "moe") -> Non
     flags = ctypes.c_int32(0)
     rc = L.gemms_moe_check(ws.data_ptr(), _stream(), ctypes.byref(flags))
     if rc != 0:
-        raise _lib.GemmsError(rc, f"device error word 0x{flags.value:x}")
+        raise _lib.GemmsError(rc, "gemms_moe_check", flags.value)
 
 
 @torch.no_grad()
@@ -176,19 +176,30 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     return out
 
 
+@torch.no_grad()
 @_on_tensor_device
 def router_logits(x: torch.Tensor, router_w: torch.Tensor) -> torch.Tensor:
-    """fp32 logits = x . router_w^T from a bf16 x and an fp32 router weight.
+    """fp32 logits = x . router_w^T from a bf16 x [T, H] and an fp32 router
+    weight [E, H], on the sm_100a router GEMM (``gemms_router_logits``).
 
-    router_w is split exactly enough into bf16 hi + lo parts (16 significant
-    bits) and both products accumulate in fp32 on the tensor cores, so the
-    result tracks an fp32 GEMM to ~1e-5 relative at bf16-GEMM cost.
+    router_w is split into bf16 hi + lo planes (16 significant bits) and both
+    products accumulate in fp32 on the tensor cores, so the result tracks an
+    fp32 GEMM to ~1e-5 relative; split-K partials are summed in a fixed order.
     """
-    w_hi = router_w.to(torch.bfloat16)
-    w_lo = (router_w - w_hi.to(torch.float32)).to(torch.bfloat16)
-    xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
-    out = torch.mm(xb, w_hi.t(), out_dtype=torch.float32)
-    out += torch.mm(xb, w_lo.t(), out_dtype=torch.float32)
+    dev = _check_cuda(x, router_w)
+    _req(x.dim() == 2 and x.dtype == torch.bfloat16, "x must be bf16 [T, H]")
+    _req(router_w.dim() == 2 and router_w.dtype == torch.float32 and router_w.shape[1] == x.shape[1],
+         "router_w must be fp32 [E, H]")
+    T, H = x.shape
+    E = router_w.shape[0]
+    L = _lib.load()
+    nbytes = L.gemms_router_workspace_size(T, H, E)
+    if nbytes == 0:
+        raise ShapeError(f"unsupported router GEMM shape (T={T} H={H} E={E}; H % 64 == 0, E <= 256)")
+    ws = _workspace(dev, nbytes, "router")
+    out = torch.empty((T, E), dtype=torch.float32, device=dev)
+    _lib.check(L.gemms_router_logits(x.data_ptr(), router_w.data_ptr(), T, H, E, out.data_ptr(), ws.data_ptr(),
+                                     nbytes, _stream()), "gemms_router_logits")
     return out
 
 
@@ -235,9 +246,9 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         _req(shared_w13.shape == (2 * I, H) and shared_w2.shape == (H, I), "shared expert shapes")
         _req(shared_w13_scale.shape == (2 * I // BLOCK, H // BLOCK), "shared_w13_scale shape")
         _req(shared_w2_scale.shape == (H // BLOCK, I // BLOCK), "shared_w2_scale shape")
-    if logits is None:
-        logits = router_logits(x, router_w)
-    _req(logits.shape == (T, E) and logits.dtype == torch.float32, "logits must be fp32 [T, E]")
+    _req(router_w.dtype == torch.float32, "router_w must be fp32")
+    if logits is not None:
+        _req(logits.shape == (T, E) and logits.dtype == torch.float32, "logits must be fp32 [T, E]")
     bias = router_bias
     out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     shape = GemmsMoeShape(T=T, H=H, I=I, E=E, E_local=E, local_expert_offset=0, n_group=n_group,
@@ -245,7 +256,8 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
                           input_mode=_lib.GEMMS_INPUT_BF16, bias_bf16=int(bias.dtype == torch.bfloat16),
                           inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor))
     args = GemmsMoeArgs()
-    args.routing_logits = _ptr(logits)
+    args.routing_logits = _ptr(logits)  # None: the router GEMM runs inside gemms_moe_fwd
+    args.router_w = _ptr(router_w)
     args.routing_bias = _ptr(bias)
     args.hidden_bf16 = _ptr(x)
     args.w13, args.w13_scale, args.w2, args.w2_scale = _ptr(w13), _ptr(w13_scale), _ptr(w2), _ptr(w2_scale)
@@ -259,6 +271,9 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
         counts = torch.empty((E,), dtype=torch.int32, device=dev)
         args.topk_idx_out, args.topk_w_out, args.expert_counts_out = _ptr(idx), _ptr(w), _ptr(counts)
+        if logits is None:
+            logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+            args.logits_out = _ptr(logits)
     ev_arr = None
     if profile_events is not None:
         ev_arr = (ctypes.c_void_p * 3)(*[e.cuda_event for e in profile_events])
@@ -268,6 +283,25 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
     if return_routing:
         return out, idx, w, counts, logits
     return out
+
+
+@torch.no_grad()
+@_on_tensor_device
+def quantize_1x128(x: torch.Tensor):
+    """Per-1x128 e4m3 quantisation of bf16 x [T, H] on the GPU
+    (``gemms_quantize_1x128``): returns (xq float8_e4m3fn [T, H], scale fp32
+    [H/128, T]) in the reference's ``hidden_states`` / ``hidden_states_scale``
+    layouts, so the pair can be passed to :func:`run`."""
+    dev = _check_cuda(x)
+    _req(x.dim() == 2 and x.dtype == torch.bfloat16, "x must be bf16 [T, H]")
+    T, H = x.shape
+    _req(H % BLOCK == 0, "H must be a multiple of 128")
+    xq = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+    sc = torch.empty((H // BLOCK, T), dtype=torch.float32, device=dev)
+    L = _lib.load()
+    _lib.check(L.gemms_quantize_1x128(x.data_ptr(), T, H, xq.data_ptr(), sc.data_ptr(), _stream()),
+               "gemms_quantize_1x128")
+    return xq, sc
 
 
 @torch.no_grad()

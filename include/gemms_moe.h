@@ -41,6 +41,15 @@ enum {
   GEMMS_ERR_CAPACITY = -9    /* a size exceeds a fixed capacity of this entry   */
 };
 
+/* Bits of the device error word (gemms_moe_check, gemms_moe_check_noalloc). */
+enum {
+  GEMMS_FLAG_PRODUCER_WAIT = 1 << 0,  /* GEMM TMA producer gave up on a free stage */
+  GEMMS_FLAG_MMA_WAIT = 1 << 1,       /* GEMM MMA thread gave up on data / TMEM    */
+  GEMMS_FLAG_EPILOGUE_WAIT = 1 << 2,  /* GEMM epilogue gave up on a partial        */
+  GEMMS_FLAG_BAD_EXPERT = 1 << 3,     /* a received row named a non-local expert   */
+  GEMMS_FLAG_ROW_OVERFLOW = 1 << 4    /* more M tiles than the workspace holds     */
+};
+
 /* Activation input formats. */
 enum {
   GEMMS_INPUT_BF16 = 0,      /* x bf16 [T,H]; quantised per 1x128 inside        */
@@ -66,7 +75,7 @@ typedef struct {
 
 typedef struct {
   GemmsMoeShape shape;
-  const float* routing_logits;      /* fp32 [T, E]                                 */
+  const float* routing_logits;      /* fp32 [T, E]; NULL: computed from router_w   */
   const void* routing_bias;         /* fp32 or bf16 [E]                            */
   const void* hidden_bf16;          /* bf16 [T, H]       (GEMMS_INPUT_BF16)        */
   const void* hidden_fp8;           /* e4m3 [T, H]       (GEMMS_INPUT_FP8)         */
@@ -86,6 +95,10 @@ typedef struct {
   void* const* profile_events;      /* optional: 3 cudaEvent_t recorded on the     */
                                     /* stream before GEMM1, between GEMM1 and      */
                                     /* GEMM2, and after GEMM2 (kernel timing)      */
+  const float* router_w;            /* fp32 [E, H]: with routing_logits NULL and   */
+                                    /* GEMMS_INPUT_BF16, logits = x . router_w^T   */
+                                    /* on the tensor cores (bf16 hi/lo split)      */
+  float* logits_out;                /* optional fp32 [T, E]: the logits used       */
 } GemmsMoeArgs;
 
 /* Bytes of device workspace gemms_moe_fwd needs for this shape. */
@@ -109,6 +122,26 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
  * overlap on the GPU (other streams, other host threads) race.  Allocates
  * nothing. */
 int gemms_moe_fwd_noalloc(const GemmsMoeArgs* args, gemms_stream_t stream);
+
+/* Router GEMM alone: logits fp32 [T, E] = x bf16 [T, H] . router_w fp32
+ * [E, H]^T (H a multiple of 64, E <= 256), computed as x . hi^T + x . lo^T
+ * with router_w = hi + lo + r split into two bf16 planes (|r| <= 2^-16 |w|)
+ * and fp32 accumulation on the tensor cores; deterministic (split-K partials
+ * are summed in a fixed order).  Workspace: gemms_router_workspace_size().
+ * No counterpart in the reference, which takes logits as input
+ * (flashinfer_baseline.py:6). */
+size_t gemms_router_workspace_size(int32_t T, int32_t H, int32_t E);
+int gemms_router_logits(const void* x_bf16, const float* router_w, int32_t T, int32_t H, int32_t E, float* logits,
+                        void* workspace, size_t ws_bytes, gemms_stream_t stream);
+
+/* Per-1x128 activation quantisation: x bf16 [T, H] -> xq e4m3 [T, H] and
+ * xq_scale fp32 [H/128, T] (the transposed layout of the reference's
+ * hidden_states_scale, flashinfer_baseline.py:59,72), scale = amax/448 (1.0
+ * for an all-zero block), xq = e4m3(x / scale) rounded to nearest even with
+ * IEEE division.  No counterpart in the reference (its run() takes quantised
+ * activations). */
+int gemms_quantize_1x128(const void* x_bf16, int32_t T, int32_t H, void* xq, float* xq_scale,
+                         gemms_stream_t stream);
 
 /* Router only (for tests and expert-parallel dispatch): fp32 logits [T,E] +
  * bias -> topk_idx int32 [T,top_k] (descending biased score), topk_w fp32
@@ -196,6 +229,25 @@ int gemms_set_gemm_ctas(int32_t max_ctas);
 /* Reads and clears the device error word kept in a gemms_moe_fwd workspace.
  * Synchronises the stream.  *flags receives the raw bit set (0 = clean). */
 int gemms_moe_check(void* workspace, gemms_stream_t stream, int32_t* flags);
+
+/* gemms_moe_check for the fixed scratch array of gemms_moe_fwd_noalloc on the
+ * current device: reads and clears its device error word (synchronises the
+ * stream).  A device-side wait that gave up inside a no-alloc call is only
+ * visible here; the next no-alloc call clears the word.  No counterpart in the
+ * reference. */
+int gemms_moe_check_noalloc(gemms_stream_t stream, int32_t* flags);
+
+/* Test hook (not for production use): from the next launch on, the producer
+ * of CTA 0 of grouped GEMM `gemm` (1 or 2) stops issuing at K iteration
+ * `k_iteration`, leaving no copy in flight, and every pipeline wait of that
+ * GEMM gives up after `wait_limit_cycles` SM cycles (0: the default ~4 s).
+ * The MMA thread's wait for the missing stage then runs out: the kernel sets
+ * bit 1 (MMA wait) of the device error word, lets its issued work drain,
+ * frees its tensor memory and returns, so the context stays usable and
+ * gemms_moe_check reports GEMMS_ERR_TIMEOUT.  gemm = 0 restores the default
+ * (no stall, default limit).  Replaces, for testing, the unbounded spins of
+ * persistent_kernel2.cu:747-757 (no counterpart). */
+int gemms_test_inject_stall(int32_t gemm, int32_t k_iteration, int64_t wait_limit_cycles);
 
 /* Static description of an error code. */
 const char* gemms_strerror(int code);

@@ -252,9 +252,19 @@ def moe_layer(x, router_w, router_bias, w13, w13_scale, w2, w2_scale,
 def compare(out: torch.Tensor, ref: torch.Tensor, rows=None) -> dict:
     """Output parity metrics used by every layer test.
 
-    ``max_rel`` = max|out-ref| / max|ref| (normwise maximum relative error) and
-    ``mae_rms`` = mean|out-ref| / RMS(ref).  The bar is max_rel <= 2e-2 and
-    mae_rms <= 1e-3.
+    * ``max_rel`` = max|out-ref| / max|ref| (normwise maximum relative error);
+    * ``mae_rms`` = mean|out-ref| / RMS(ref);
+    * ``elem_rel`` = max over elements with |ref| >= 1e-2 max|ref| of
+      |out-ref| / |ref| (elementwise relative error), and ``elem_rel_10`` the
+      same over |ref| >= 1e-1 max|ref|;
+    * ``elem_frac`` = the share of elements that ``elem_rel`` covers.
+
+    The bars (tests/helpers.py) are max_rel <= 2e-2 and mae_rms <= 1e-3 (the
+    BASELINE north star), elem_rel_10 <= 2e-2 and elem_rel <= 1e-1.  A bf16
+    output is only resolved to 2^-8 relative, so an element one rounding step
+    off already reads 0.4-0.8% here; elements near 1% of the maximum move by
+    a few steps under the fp8 intermediate's rounding (about 4% in a CPU
+    emulation of the GPU arithmetic at config c0).
     """
     o = out.to(torch.float64)
     r = ref.to(torch.float64)
@@ -262,8 +272,18 @@ def compare(out: torch.Tensor, ref: torch.Tensor, rows=None) -> dict:
         idx = torch.as_tensor(rows, dtype=torch.long)
         o, r = o.index_select(0, idx), r.index_select(0, idx)
     d = (o - r).abs()
+    ra = r.abs()
+    amax = ra.max().clamp_min(1e-30)
     rms = r.pow(2).mean().sqrt().clamp_min(1e-30)
-    return {"max_rel": float(d.max() / r.abs().max().clamp_min(1e-30)),
+
+    def elem(th):
+        big = ra >= th * amax
+        return float((d[big] / ra[big]).max()) if bool(big.any()) else 0.0
+
+    return {"max_rel": float(d.max() / amax),
             "mae_rms": float(d.mean() / rms),
+            "elem_rel": elem(1e-2),
+            "elem_rel_10": elem(1e-1),
+            "elem_frac": float((ra >= 1e-2 * amax).double().mean()),
             "max_abs": float(d.max()),
             "rms": float(rms)}

@@ -14,6 +14,12 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref
 # Parity bar: normwise max relative error and MAE/RMS.
 MAX_REL = 2e-2
 MAE_RMS = 1e-3
+# Elementwise relative error (oracle/reference_moe.py: compare): over elements
+# >= 10% of max|ref| the north-star 2e-2 applies per element; over elements
+# >= 1% of max|ref| a bf16 output a few rounding steps off reads up to ~4%
+# (CPU emulation of the GPU arithmetic), so the bar there is 1e-1.
+ELEM_REL_10 = 2e-2
+ELEM_REL = 1e-1
 
 
 def load_golden():
@@ -40,8 +46,13 @@ def sorted_sets(idx: torch.Tensor) -> torch.Tensor:
 
 
 def assert_parity(out: torch.Tensor, ref: torch.Tensor, what: str = "", rows=None):
+    """Asserts the layer parity bar and prints every metric (normwise and
+    elementwise) so that each test's log shows both."""
     m = R.compare(out.cpu(), ref.cpu(), rows=rows)
+    print(f"{what}: max_rel {m['max_rel']:.3e} mae_rms {m['mae_rms']:.3e} elem_rel {m['elem_rel']:.3e} "
+          f"elem_rel_10 {m['elem_rel_10']:.3e} (elements covered {m['elem_frac']:.3f})")
     assert m["max_rel"] <= MAX_REL and m["mae_rms"] <= MAE_RMS, f"{what} parity failed: {m}"
+    assert m["elem_rel_10"] <= ELEM_REL_10 and m["elem_rel"] <= ELEM_REL, f"{what} elementwise parity failed: {m}"
     return m
 
 

@@ -125,3 +125,17 @@ def test_new_entry_points_validate_arguments_without_gpu():
     assert L.gemms_set_gemm_ctas(-1) == ERR_ARG
     prev = L.gemms_set_gemm_ctas(7)
     assert L.gemms_set_gemm_ctas(prev) == 7
+
+
+def test_stall_hook_rejects_bad_arguments():
+    """gemms_test_inject_stall validates its arguments on the host."""
+    L = gemms_b200.load_library()
+    assert L.gemms_test_inject_stall(3, 0, 0) == -8
+    assert L.gemms_test_inject_stall(1, -1, 0) == -8
+    assert L.gemms_test_inject_stall(1, 0, -5) == -8
+    assert L.gemms_test_inject_stall(0, 0, 0) == 0
+
+
+def test_noalloc_check_rejects_null_flags():
+    L = gemms_b200.load_library()
+    assert L.gemms_moe_check_noalloc(None, None) == -8

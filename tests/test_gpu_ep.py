@@ -46,18 +46,37 @@ def _worker(rank, world, port, outdir, case, combine="nccl"):
     kw = dict(n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k, routed_scaling_factor=sh.rsf,
               shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
               shared_w2_scale=d["shared_w2_scale"])
+    wts = (d["w13"][el].contiguous(), d["w13_scale"][el].contiguous(), d["w2"][el].contiguous(),
+           d["w2_scale"][el].contiguous())
     for _ in range(2):  # second call reuses the cached workspaces
-        out = gemms_b200.moe(d["x"][sl].contiguous(), d["router_w"], d["router_bias"], d["w13"][el].contiguous(),
-                             d["w13_scale"][el].contiguous(), d["w2"][el].contiguous(),
-                             d["w2_scale"][el].contiguous(), ep_group=dist.group.WORLD, **kw)
+        out = gemms_b200.moe(d["x"][sl].contiguous(), d["router_w"], d["router_bias"], *wts,
+                             ep_group=dist.group.WORLD, **kw)
     torch.cuda.synchronize()
     torch.save(out.cpu(), os.path.join(outdir, f"ep{rank}.pt"))
+    # A run of calls with different token counts and inputs (so different
+    # routing): the peer combine alternates between two symmetric buffers and
+    # a rank rewrites buffer i % 2 while relying on call i - 1's barrier for
+    # the peers' reads of call i - 2; the last call needs more rows than any
+    # before it and grows the buffers.  Each call is checked against the
+    # single-GPU layer on the same tokens.
+    seq = []
+    for i, tpr in enumerate((T, T // 2, T // 4, T // 2, T, 2 * T)):
+        g = torch.Generator(device=dev).manual_seed(100 + i)
+        x_all = torch.randn((world * tpr, sh.H), generator=g, device=dev).to(torch.bfloat16)
+        o = gemms_b200.moe(x_all[rank * tpr:(rank + 1) * tpr].contiguous(), d["router_w"], d["router_bias"], *wts,
+                           ep_group=dist.group.WORLD, **kw)
+        seq.append((x_all, o))
+    torch.cuda.synchronize()
+    torch.save([o.cpu() for _, o in seq], os.path.join(outdir, f"seq{rank}.pt"))
     if rank == 0:
         single, idx, w, counts, logits = gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"],
                                                         d["w13_scale"], d["w2"], d["w2_scale"], return_routing=True,
                                                         **kw)
+        seq_single = [gemms_b200.moe(x_all, d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"],
+                                     d["w2_scale"], **kw).cpu() for x_all, _ in seq]
         torch.cuda.synchronize()
-        torch.save({"single": single.cpu(), "logits": logits.cpu()}, os.path.join(outdir, "single.pt"))
+        torch.save({"single": single.cpu(), "logits": logits.cpu(), "seq": seq_single},
+                   os.path.join(outdir, "single.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -75,7 +94,13 @@ def test_ep2_matches_single_gpu_and_oracle(case, combine):
     with tempfile.TemporaryDirectory() as tmp:
         mp.spawn(_worker, args=(world, _free_port(), tmp, case, combine), nprocs=world, join=True)
         ep = torch.cat([torch.load(os.path.join(tmp, f"ep{r}.pt")) for r in range(world)])
+        seqs = [torch.load(os.path.join(tmp, f"seq{r}.pt")) for r in range(world)]
         s = torch.load(os.path.join(tmp, "single.pt"))
+    for i, want in enumerate(s["seq"]):
+        got = torch.cat([seqs[r][i] for r in range(world)])
+        mi = R.compare(got, want)
+        print(f"EP2 {case} {combine} call {i} ({got.shape[0]} tokens) vs single GPU", mi)
+        assert mi["mae_rms"] < 3e-4 and mi["max_rel"] < 1e-2, f"call {i}: {mi}"
     m = R.compare(ep, s["single"])
     # The combine rows travel as fp16 with an exact power-of-two scale (2^-11
     # relative), which flips a few bf16 output roundings against the single-GPU

@@ -123,62 +123,106 @@ def _cpu_weights_for(d_dev, experts):
     return out
 
 
+def _full_layer(sh, d, **extra):
+    return gemms_b200.moe(
+        d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+        shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
+        shared_w2_scale=d["shared_w2_scale"], n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k,
+        routed_scaling_factor=sh.rsf, return_routing=True, **extra)
+
+
+def _check_routing(sh, idx, counts, lg, bias):
+    ridx, _, _, _ = R.route(lg, bias, sh.n_group, sh.topk_group, sh.top_k, sh.rsf)
+    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
+    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=sh.E))
+    assert int(counts.sum()) == sh.T * sh.top_k
+    return ridx
+
+
 @pytest.mark.slow
-def test_moe_c1_full_size_sampled_tokens():
-    """Config c1 (T=4096, full V3 + shared expert): routing of all tokens exact,
-    output rows of a token sample within the parity bar."""
+def test_moe_c1_all_rows():
+    """Config c1 (T=4096, full V3 + shared expert): routing of all tokens exact
+    and every one of the 4096 output rows within the parity bar (the oracle
+    runs the whole layer on the host cores)."""
     sh = W.CONFIGS["c1"]
     d = W.make_inputs(sh, seed=0, device="cuda")
-    out, idx, w, counts, logits = gemms_b200.moe(
-        d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
-        shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
-        shared_w2_scale=d["shared_w2_scale"], return_routing=True)
+    out, idx, w, counts, logits = _full_layer(sh, d)
     gemms_b200.check_device_errors(tag="moe")
     lg = logits.cpu()
-    bias = d["router_bias"].cpu()
-    ridx, _, _, _ = R.route(lg, bias, 8, 4, 8, 2.5)
-    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
-    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=256))
-    assert int(counts.sum()) == 4096 * 8
-    rows = [0, 1, 777, 2048, 4095]
-    experts = sorted(set(ridx[rows].reshape(-1).tolist()))
-    cw = _cpu_weights_for(d, experts)
-    x = d["x"].cpu()
-    ref = R.moe_layer(x, d["router_w"].cpu(), bias, cw["w13"], cw["w13_scale"], cw["w2"], cw["w2_scale"],
-                      d["shared_w13"].cpu(), d["shared_w13_scale"].cpu(), d["shared_w2"].cpu(),
-                      d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg,
-                      tokens=rows)
-    m = Hh.assert_parity(out, ref, "c1 sampled", rows=rows)
-    print("c1 sampled parity", m)
-    o = out.float()
-    assert torch.isfinite(o).all()
+    cpu = {k: v.cpu() for k, v in d.items()}
+    _check_routing(sh, idx, counts, lg, cpu["router_bias"])
+    ref = R.moe_layer(cpu["x"], cpu["router_w"], cpu["router_bias"], cpu["w13"], cpu["w13_scale"], cpu["w2"],
+                      cpu["w2_scale"], cpu["shared_w13"], cpu["shared_w13_scale"], cpu["shared_w2"],
+                      cpu["shared_w2_scale"], n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg)
+    Hh.assert_parity(out, ref, "c1 all 4096 rows")
+    assert torch.isfinite(out.float()).all()
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("T", [1, 8])
+@pytest.mark.parametrize("T", [1, 8, 32, 128])
 def test_moe_decode_full_size(T):
     """Config c2 (decode, full V3 + shared expert): every token checked against
-    the oracle; almost every expert gets 0 or 1 rows, so each M tile is nearly
-    empty and the tile planning / padding rows are exercised."""
+    the oracle.  At T=1/8 almost every expert gets 0 or 1 rows (nearly empty M
+    tiles); at T=32/128 tiles start to fill."""
     sh = W.CONFIGS["c2"].replace(T=T)
     d = W.make_inputs(sh, seed=7, device="cuda")
-    out, idx, w, counts, logits = gemms_b200.moe(
-        d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
-        shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
-        shared_w2_scale=d["shared_w2_scale"], return_routing=True)
+    out, idx, w, counts, logits = _full_layer(sh, d)
     gemms_b200.check_device_errors(tag="moe decode")
     lg = logits.cpu()
     bias = d["router_bias"].cpu()
-    ridx, _, _, _ = R.route(lg, bias, 8, 4, 8, 2.5)
-    assert torch.equal(Hh.sorted_sets(idx), Hh.sorted_sets(ridx))
-    assert torch.equal(counts.cpu().long(), torch.bincount(ridx.reshape(-1), minlength=256))
+    ridx = _check_routing(sh, idx, counts, lg, bias)
     experts = sorted(set(ridx.reshape(-1).tolist()))
     cw = _cpu_weights_for(d, experts)
     ref = R.moe_layer(d["x"].cpu(), d["router_w"].cpu(), bias, cw["w13"], cw["w13_scale"], cw["w2"],
                       cw["w2_scale"], d["shared_w13"].cpu(), d["shared_w13_scale"].cpu(), d["shared_w2"].cpu(),
                       d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg)
-    m = Hh.assert_parity(out, ref, f"c2 T={T}")
-    print(f"c2 T={T} parity", m)
+    Hh.assert_parity(out, ref, f"c2 T={T}")
+
+
+@pytest.mark.slow
+def test_moe_c4_skewed_routing():
+    """Config c4's skewed routing (router bias calibrated so expert popularity
+    follows Zipf(1.2), hottest experts in groups 0-1) on one GPU with all 256
+    experts and T=16384: routing sets and counts exact; output rows of tokens
+    sampled across the M-tile boundaries of the two hottest experts (thousands
+    of rows each, tens of 128-row tiles, a ragged tail tile) within the bar."""
+    sh = W.CONFIGS["c4"]
+    d = W.make_inputs(sh, seed=3, device="cuda")
+
+    def route_fn(lg, b):
+        return gemms_b200.route(lg, b, n_group=sh.n_group, topk_group=sh.topk_group, top_k=sh.top_k,
+                                routed_scaling_factor=sh.rsf, counts=False)[0]
+
+    bias, frac = W.zipf_bias(sh, route_fn, router_w=d["router_w"], s=1.2, seed=0, hot_ranks=2, world=8,
+                             device="cuda")
+    d["router_bias"] = bias
+    out, idx, w, counts, logits = _full_layer(sh, d)
+    gemms_b200.check_device_errors(tag="moe c4")
+    lg = logits.cpu()
+    cbias = bias.cpu()
+    ridx = _check_routing(sh, idx, counts, lg, cbias)
+    c = counts.cpu().long()
+    hot = torch.argsort(c, descending=True)[:2].tolist()
+    print("c4 hottest experts", hot, "rows", [int(c[e]) for e in hot], "share of top expert",
+          float(c.max()) / float(c.sum()))
+    assert int(c[hot[0]]) > 4 * 128  # several M tiles
+    rows = set()
+    for e in hot:
+        toks = torch.nonzero((ridx == e).any(1)).squeeze(1)  # token order = row order within the expert
+        n = toks.numel()
+        for pos in (0, 1, 127, 128, 129, 255, 256, n // 2, n - 129, n - 128, n - 2, n - 1):
+            if 0 <= pos < n:
+                rows.add(int(toks[pos]))
+    g = torch.Generator().manual_seed(0)
+    rows |= set(torch.randint(0, sh.T, (6,), generator=g).tolist())
+    rows = sorted(rows)
+    experts = sorted(set(ridx[rows].reshape(-1).tolist()))
+    cw = _cpu_weights_for(d, experts)
+    ref = R.moe_layer(d["x"].cpu(), d["router_w"].cpu(), cbias, cw["w13"], cw["w13_scale"], cw["w2"],
+                      cw["w2_scale"], d["shared_w13"].cpu(), d["shared_w13_scale"].cpu(), d["shared_w2"].cpu(),
+                      d["shared_w2_scale"].cpu(), n_group=8, topk_group=4, top_k=8, rsf=2.5, logits=lg,
+                      tokens=rows)
+    Hh.assert_parity(out, ref, f"c4 skewed, {len(rows)} sampled rows", rows=rows)
 
 
 def test_gemm_cta_bound_keeps_results():

@@ -64,3 +64,41 @@ def test_router_large_logits_saturate():
     logits = torch.randn(64, 256, generator=g) * 60
     bias = (torch.rand(256, generator=g) - 0.5) * 0.2
     _check(logits, bias, 8, 4, 8)
+
+
+def _logits_err(got, ref):
+    d = (got.double() - ref.double()).abs()
+    return float(d.max() / ref.double().abs().max())
+
+
+@pytest.mark.parametrize("cfg,T", [("c0", 64), ("c1", 4096), ("c1", 1), ("c1", 130), ("c2", 32)])
+def test_router_gemm_matches_fp32(cfg, T):
+    """The sm_100a router GEMM (bf16 hi/lo split of router_w, fp32 accumulation
+    on the tensor cores) against the oracle's fp32 x . router_w^T: normwise
+    relative error <= 1e-5, elementwise within rtol 1e-4 / atol 2e-5; two calls
+    give identical bits (split-K partials summed in a fixed order); the CUDA
+    router fed these logits routes exactly like the oracle fed them."""
+    sh = W.CONFIGS[cfg].replace(T=T)
+    d = W.make_inputs(sh, seed=13, with_weights=False)
+    x, rw = d["x"].cuda(), d["router_w"].cuda()
+    got = gemms_b200.router_logits(x, rw)
+    again = gemms_b200.router_logits(x, rw)
+    torch.cuda.synchronize()
+    ref = R.router_logits(d["x"], d["router_w"])
+    err = _logits_err(got.cpu(), ref)
+    print(f"{cfg} T={T}: router GEMM normwise rel err {err:.2e}")
+    assert err <= 1e-5
+    torch.testing.assert_close(got.cpu(), ref, rtol=1e-4, atol=2e-5)
+    assert torch.equal(got, again)
+    _check(got.cpu(), d["router_bias"], sh.n_group, sh.topk_group, sh.top_k)
+
+
+def test_router_gemm_small_expert_count():
+    """E not a multiple of 16 (MMA N padded with zero weight rows)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(77, 256, generator=g).bfloat16()
+    rw = torch.randn(24, 256, generator=g) * 0.02
+    got = gemms_b200.router_logits(x.cuda(), rw.cuda()).cpu()
+    ref = R.router_logits(x, rw)
+    assert _logits_err(got, ref) <= 1e-5
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=2e-5)

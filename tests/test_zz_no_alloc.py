@@ -27,11 +27,7 @@ MAX_REL, MAE_RMS = 2e-2, 1e-3  # the layer parity bar used by every test
 
 def _entry_points():
     L = _lib.load()
-    fwd = L.gemms_moe_fwd
-    noalloc = L.gemms_moe_fwd_noalloc
-    noalloc.argtypes = [ctypes.POINTER(GemmsMoeArgs), ctypes.c_void_p]
-    noalloc.restype = ctypes.c_int32
-    return L, fwd, noalloc
+    return L, L.gemms_moe_fwd, L.gemms_moe_fwd_noalloc
 
 
 def _make_args(sh, d, logits, out, idx):
@@ -81,6 +77,46 @@ def test_noalloc_matches_workspace_entry_point(cfg, T):
         assert torch.equal(idx, ref_idx), f"call {call}: routing differs from gemms_moe_fwd"
         m = R.compare(out.cpu(), ref.cpu())
         assert m["max_rel"] <= MAX_REL and m["mae_rms"] <= MAE_RMS, f"call {call}: {m}"
+    flags = ctypes.c_int32(-1)
+    assert L.gemms_moe_check_noalloc(stream, ctypes.byref(flags)) == 0
+    assert flags.value == 0
+
+
+def test_noalloc_reports_an_expired_device_wait():
+    """A device-side wait that runs out inside a no-alloc call (forced with the
+    test hook) is reported by gemms_moe_check_noalloc, which also clears it;
+    the next call is clean and matches the workspace entry point."""
+    sh = W.CONFIGS["c0"].replace(T=16, shared=True)
+    d = W.make_inputs(sh, seed=22, device="cuda")
+    logits = gemms_b200.router_logits(d["x"], d["router_w"])
+    L, fwd, noalloc = _entry_points()
+    stream = torch.cuda.current_stream().cuda_stream
+    ref = torch.empty((sh.T, sh.H), dtype=torch.bfloat16, device="cuda")
+    ref_idx = torch.empty((sh.T, sh.top_k), dtype=torch.int32, device="cuda")
+    shape, a = _make_args(sh, d, logits, ref, ref_idx)
+    nbytes = L.gemms_moe_workspace_size(ctypes.byref(shape))
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device="cuda")
+    assert fwd(ctypes.byref(a), ws.data_ptr() + ((-ws.data_ptr()) % 256), nbytes, stream) == 0
+
+    out = torch.empty((sh.T, sh.H), dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty((sh.T, sh.top_k), dtype=torch.int32, device="cuda")
+    _, b = _make_args(sh, d, logits, out, idx)
+    assert L.gemms_test_inject_stall(1, 2, 2_000_000) == 0
+    try:
+        assert noalloc(ctypes.byref(b), stream) == 0
+        torch.cuda.synchronize()
+    finally:
+        assert L.gemms_test_inject_stall(0, 0, 0) == 0
+    flags = ctypes.c_int32(0)
+    assert L.gemms_moe_check_noalloc(stream, ctypes.byref(flags)) == _lib.GEMMS_ERR_TIMEOUT
+    assert flags.value & _lib.FLAG_MMA_WAIT, hex(flags.value)
+    assert L.gemms_moe_check_noalloc(stream, ctypes.byref(flags)) == 0 and flags.value == 0  # cleared
+
+    assert noalloc(ctypes.byref(b), stream) == 0
+    assert L.gemms_moe_check_noalloc(stream, ctypes.byref(flags)) == 0 and flags.value == 0
+    assert torch.equal(idx, ref_idx)
+    m = R.compare(out.cpu(), ref.cpu())
+    assert m["max_rel"] <= MAX_REL and m["mae_rms"] <= MAE_RMS, m
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch():
