@@ -9,12 +9,18 @@
 // Design (one persistent CTA per SM, 384 threads, warp-specialised; the
 // control warpgroup 0-3 runs on 40-56 registers, the epilogue warpgroups on
 // 224-232 via setmaxnreg):
-//   warp 0      TMA producer: A tile(s) [128 rows x 128 B] per plane and two
-//               128-row weight boxes per stage into a 2-4 deep smem ring.
+//   warp 0      TMA producer: two 128-row weight boxes and the A tile(s)
+//               [128 rows x 128 B] per stage into a 2-4 deep smem ring.  GEMM1
+//               gathers its A rows straight from the token-major activations
+//               (each lane issues one tile::gather4 of four rows), so no
+//               per-expert copy of the activations is ever written; GEMM2
+//               loads the intermediate (already grouped) as tiles.
 //   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
 //               (M=128, N=256, K=32 e4m3) from one thread; each 128-wide K
 //               block goes to one of two TMEM partial accumulators.
-//   warps 2-3   idle (setmaxnreg works per warpgroup).
+//   warp 2      GEMM1 only: gathers the A rows (tile::gather4, four rows per
+//               lane) into the same stages.
+//   warp 3      idle (setmaxnreg works per warpgroup).
 //   warps 4-11  "promotion" epilogue: for every K block read the fp32 partial
 //               from TMEM, multiply by a_scale[row,kb] * w_scale[nblk,kb] and
 //               accumulate in registers (the block scales are arbitrary fp32,
@@ -87,9 +93,13 @@ struct GemmParams {
   int w_rows;        // weight rows per expert
   int b_row_step;    // weight rows per N tile step
   int b_row_hi;      // row offset of the second 128-row weight box
-  int prefetch;      // weight K-blocks prefetched into L2 ahead of the smem ring
+  // A operand rows: GEMM1 gathers source row a_src[r] for grouped row r
+  // (nullptr: r itself); the scale of (source row q, K block kb) is
+  // a_scale[kb * a_kb_stride + q * a_src_stride].
+  const int32_t* a_src;
   const float* a_scale;
-  int a_scale_ld;
+  int a_kb_stride;
+  int a_src_stride;
   const float* w_scale;   // [E, w_rows/128, kb_count]
   const float* sw_scale;  // [w_rows/128, kb_count]
   // GEMM1 epilogue
@@ -143,12 +153,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* amax_x = reinterpret_cast<float*>(smem + C::kRingBytes + 512);  // [2 units][2 halves][128]
+  int* gidx = reinterpret_cast<int*>(smem + C::kRingBytes + 2560);       // GEMM1: [128] gather rows
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], MODE == 0 ? 2 : 1);  // GEMM1: weight producer + row-gather warp
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -180,70 +191,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kEpiFirstWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(Regs<MODE>::ctrl));
-   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_a = policy_evict_last();
-      // Weight coordinates of this CTA's it-th K iteration (units are strided
-      // by gridDim.x); used both to load and to prefetch ahead into L2.
-      const int my_units = total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-      const int my_iters = my_units * p.kb_count;
-      auto weight_rows = [&](int it, int& kb, int& wrow, const CUtensorMap*& mb) {
-        const int i = it / p.kb_count;
-        kb = it - i * p.kb_count;
-        const int u = blockIdx.x + i * gridDim.x;
-        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
-        const int g = p.tile_group[mt];
-        const bool sh = (g == p.shared_group);
-        mb = sh ? &tmBs : &tmB;
-        wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
-      };
-      for (int pf = 0; pf < p.prefetch && pf < my_iters; ++pf) {
-        int kb, wrow;
-        const CUtensorMap* mb;
-        weight_rows(pf, kb, wrow, mb);
-        tma_prefetch_l2_2d(mb, kb * BK, wrow, pol_w);
-        tma_prefetch_l2_2d(mb, kb * BK, wrow + p.b_row_hi, pol_w);
-      }
-      int it = 0;
-      for (int u = blockIdx.x; u < total; u += gridDim.x) {
-        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
-        const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
-        const bool sh = (g == p.shared_group);
-        const CUtensorMap* mb = sh ? &tmBs : &tmB;
-        const int wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
-        bool ok = true;
-        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t round = it / S;
-          if (p.prefetch > 0 && it + p.prefetch < my_iters) {
-            int pkb, pwrow;
-            const CUtensorMap* pmb;
-            weight_rows(it + p.prefetch, pkb, pwrow, pmb);
-            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow, pol_w);
-            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow + p.b_row_hi, pol_w);
-          }
-          if (blockIdx.x == 0 && it == p.stall_iter) {
-            ok = false;  // test hook: withhold this stage (no expect_tx, no loads)
-            break;
-          }
-          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait, p.wait_limit)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+   if (warp == 0 || (MODE == 0 && warp == 2)) {
+    // ------------------------------------------------------------ producers
+    // Warp 0, lane 0: waits for a free stage, arms the stage barrier with the
+    // bytes it loads and loads the two weight boxes (GEMM2 also its A tiles).
+    // GEMM1 only, warp 2: waits for the same stage, arms the barrier with the
+    // A tile's bytes and gathers the tile's 128 A rows, four per lane
+    // (tile::gather4).  Each stage barrier therefore expects one arrival per
+    // producer warp.  Both warps stop at the same K iteration under the test
+    // hook; a timeout stops either early (the drain below is bounded).
+    const bool gather = (MODE == 0 && warp == 2);
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+      const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
+      if (gather) {
+        // the tile's 128 source rows, staged once per unit; rows past the
+        // tile's count repeat its last row (loaded, never stored)
+        const int last = p.tile_rows[mt] - 1;
+        __syncwarp();  // previous unit's reads of gidx are done
 #pragma unroll
-          for (int pl = 0; pl < PLANES; ++pl)
-            tma_load_2d(st + pl * kTileA, &tmA, &full[s], pl * p.plane_stride + kb * BK, row0, pol_a);
+        for (int j = 0; j < 4; ++j) {
+          const int rr = row0 + min(32 * j + lane, last);
+          gidx[32 * j + lane] = p.a_src ? __ldg(p.a_src + rr) : rr;
+        }
+        __syncwarp();
+      }
+      for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+        const int s = it % S;
+        const uint32_t round = it / S;
+        int go = 1;
+        if (lane == 0) {
+          if (blockIdx.x == 0 && it == p.stall_iter)
+            go = 0;  // test hook: withhold this stage (no expect_tx, no loads)
+          else
+            go = mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait, p.wait_limit);
+        }
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (!go) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * C::kStageBytes;
+        if (gather) {
+          if (lane == 0) mbar_arrive_expect_tx(&full[s], kTileA);
+          __syncwarp();
+          const int4 src = *reinterpret_cast<const int4*>(gidx + 4 * lane);
+          tma_gather4(st + lane * 4 * BK, &tmA, &full[s], kb * BK, src.x, src.y, src.z, src.w, policy_evict_last());
+        } else if (lane == 0) {
+          const bool sh = (g == p.shared_group);
+          const CUtensorMap* mb = sh ? &tmBs : &tmB;
+          const int wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes - (MODE == 0 ? kTileA : 0));
+          if (MODE != 0) {
+            const uint64_t pol_a = policy_evict_last();
+#pragma unroll
+            for (int pl = 0; pl < PLANES; ++pl)
+              tma_load_2d(st + pl * kTileA, &tmA, &full[s], pl * p.plane_stride + kb * BK, row0, pol_a);
+          }
+          const uint64_t pol_w = policy_evict_first();
           uint8_t* sb = st + PLANES * kTileA;
           tma_load_2d(sb, mb, &full[s], kb * BK, wrow, pol_w);
           tma_load_2d(sb + kTileA, mb, &full[s], kb * BK, wrow + p.b_row_hi, pol_w);
         }
-        if (!ok) break;
       }
-      // Let every copy this thread issued land before the CTA can exit.
+    }
+    // Let every copy this warp issued land before the CTA can exit.
+    if (lane == 0) {
       for (int s = 0; s < S && s < it; ++s) {
         const int last = s + S * ((it - 1 - s) / S);
         mbar_wait_drain(&full[s], (last / S) & 1);
@@ -339,7 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Scales are prefetched three K blocks ahead (global-load latency is
       // ~1 pipeline iteration under load).  Rows past the tile's valid count
       // read row 0's scale and are never stored.
-      const float* a_sc = p.a_scale + row0 + (valid ? r : 0);
+      const int arow = row0 + (valid ? r : 0);
+      const int asrc = (MODE == 0 && p.a_src) ? __ldg(p.a_src + arow) : arow;
+      const float* a_sc = p.a_scale + (size_t)asrc * p.a_src_stride;
       const float* w0p = ws + (size_t)blk0 * p.kb_count;
       const float* w1p = ws + (size_t)blk1 * p.kb_count;
       float acc[128];
@@ -349,12 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       float as0 = __ldg(a_sc), w00 = __ldg(w0p), w10 = __ldg(w1p);
       float as1 = 0.f, w01 = 0.f, w11 = 0.f, as2 = 0.f, w02 = 0.f, w12 = 0.f;
       if (KB > 1) {
-        as1 = __ldg(a_sc + (size_t)p.a_scale_ld);
+        as1 = __ldg(a_sc + (size_t)p.a_kb_stride);
         w01 = __ldg(w0p + 1);
         w11 = __ldg(w1p + 1);
       }
       if (KB > 2) {
-        as2 = __ldg(a_sc + 2 * (size_t)p.a_scale_ld);
+        as2 = __ldg(a_sc + 2 * (size_t)p.a_kb_stride);
         w02 = __ldg(w0p + 2);
         w12 = __ldg(w1p + 2);
       }
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         as0 = as1; w00 = w01; w10 = w11;
         as1 = as2; w01 = w02; w11 = w12;
         if (kb + 3 < KB) {
-          as2 = __ldg(a_sc + (size_t)(kb + 3) * p.a_scale_ld);
+          as2 = __ldg(a_sc + (size_t)(kb + 3) * p.a_kb_stride);
           w02 = __ldg(w0p + kb + 3);
           w12 = __ldg(w1p + kb + 3);
         }
@@ -514,20 +531,6 @@ void apply_wait_knobs(GemmParams& p, int gemm) {
                                                                         : -1;
 }
 
-// Weight K-blocks a CTA keeps in flight toward L2 beyond its smem ring.  The
-// weight stream is DRAM-latency bound (one 32 KB stage per K-block per SM);
-// GEMMS_PREFETCH overrides the default for tuning.
-int prefetch_depth() {
-  static int depth = -1;
-  if (depth < 0) {
-    const char* e = getenv("GEMMS_PREFETCH");
-    depth = e ? atoi(e) : 0;
-    if (depth < 0) depth = 0;
-    if (depth > 64) depth = 64;
-  }
-  return depth;
-}
-
 // 2-D uint8 tensor [rows, inner] with a 128x128 box and 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride) {
   auto fn = encode_fn();
@@ -536,6 +539,22 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, ui
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {row_stride};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(BM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GEMMS_OK : GEMMS_ERR_DRIVER;
+}
+
+// 2-D uint8 tensor [rows, inner] with a one-row, 128-byte box (128-byte
+// swizzle), for tile::gather4 row gathers.
+int make_gather_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride) {
+  auto fn = encode_fn();
+  if (!fn) return GEMMS_ERR_DRIVER;
+  if (!aligned16(base) || (row_stride % 16) || inner % BK) return GEMMS_ERR_ALIGN;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 1u};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -584,7 +603,8 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
   CUtensorMap ma, mb, mbs;
   int rc;
-  if ((rc = make_map(&ma, a.a, a.H, a.a_rows, a.H))) return rc;
+  if (a.a_rows <= 0 || a.a_row_stride < a.H) return GEMMS_ERR_SHAPE;
+  if ((rc = make_gather_map(&ma, a.a, a.H, a.a_rows, a.a_row_stride))) return rc;
   if ((rc = make_map(&mb, a.w13, a.H, (uint64_t)a.E_local * 2 * a.I, a.H))) return rc;
   if (a.sw13) {
     if ((rc = make_map(&mbs, a.sw13, a.H, 2ull * a.I, a.H))) return rc;
@@ -604,9 +624,10 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.w_rows = 2 * a.I;
   p.b_row_step = kBlock;
   p.b_row_hi = a.I;
-  p.prefetch = prefetch_depth();
+  p.a_src = a.a_src;
   p.a_scale = a.a_scale;
-  p.a_scale_ld = a.a_scale_ld;
+  p.a_kb_stride = static_cast<int>(a.a_scale_kb_stride);
+  p.a_src_stride = static_cast<int>(a.a_scale_src_stride);
   p.w_scale = a.w13_scale;
   p.sw_scale = a.sw13_scale;
   p.inter = a.inter;
@@ -646,9 +667,10 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.w_rows = a.H;
   p.b_row_step = BN;
   p.b_row_hi = kBlock;
-  p.prefetch = prefetch_depth();
+  p.a_src = nullptr;
   p.a_scale = a.inter_scale;
-  p.a_scale_ld = a.inter_scale_ld;
+  p.a_kb_stride = a.inter_scale_ld;
+  p.a_src_stride = 1;
   p.w_scale = a.w2_scale;
   p.sw_scale = a.sw2_scale;
   p.row_dest = a.row_dest;

@@ -123,12 +123,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Prefetch a 2-D tile into L2 (no shared memory, no completion tracking).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y, uint64_t policy) {
+// Row gather: four rows (y0..y3) of a 2-D tensor whose tensor map has a box
+// one row high, columns [x, x + box width), into four consecutive box rows
+// at `dst` (same swizzle as a tiled load to that address), completing on
+// `bar`.  No multicast.  x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y0,
+                                            int y1, int y2, int y3, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(x), "r"(y), "l"(policy)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3),
+      "l"(policy)
       : "memory");
 }
 

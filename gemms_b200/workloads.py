@@ -169,4 +169,8 @@ def zipf_bias(shape: MoeShape, route_fn, router_w: torch.Tensor | None = None, s
         hist = torch.bincount(idx.reshape(-1).long(), minlength=E).double()
         frac = hist / hist.sum()
         bias = bias + (0.05 * torch.log((target + 1e-6) / (frac + 1e-6))).float().clamp(-0.2, 0.2)
+        # Routing is invariant to a common offset of the bias; keep it centred
+        # so that sigmoid + bias stays near 1, where fp32 resolves the scores
+        # finely (an offset of ~3 leaves 4x coarser spacing and more near-ties).
+        bias = bias - bias.mean()
     return bias, frac

@@ -43,7 +43,7 @@ def test_workspace_size_and_shape_rejection():
     s = _lib.GemmsMoeShape(T=4096, H=7168, I=2048, E=256, E_local=256, n_group=8, topk_group=4, top_k=8,
                            has_shared=1, input_mode=0, inter_planes=2, routed_scaling_factor=2.5)
     n = L.gemms_moe_workspace_size(ctypes.byref(s))
-    assert 400e6 < n < 700e6
+    assert 200e6 < n < 700e6
     bad = _lib.GemmsMoeShape(**{f: getattr(s, f) for f, _ in _lib.GemmsMoeShape._fields_})
     bad.n_group = 7  # 256 % 7 != 0
     assert L.gemms_moe_workspace_size(ctypes.byref(bad)) == 0

@@ -20,9 +20,12 @@ def _inputs(T, H, seed):
     # blocks of very different magnitudes, an all-zero block, values that
     # quantise to exactly +-448, subnormal e4m3 outputs
     x[:, :128] *= 1e-3
-    x[0, 128:256] = 0
-    x[1, 256:384] = torch.linspace(-1, 1, 128)
-    x[2, 384:512] *= 1e4
+    if H >= 512:
+        x[0, 128:256] = 0
+        x[min(1, T - 1), 256:384] = torch.linspace(-1, 1, 128)
+        x[min(2, T - 1), 384:512] *= 1e4
+    else:
+        x[0, 128:256] = 0
     return x.to(torch.bfloat16)
 
 

@@ -75,7 +75,9 @@ def _logits_err(got, ref):
 def test_router_gemm_matches_fp32(cfg, T):
     """The sm_100a router GEMM (bf16 hi/lo split of router_w, fp32 accumulation
     on the tensor cores) against the oracle's fp32 x . router_w^T: normwise
-    relative error <= 1e-5, elementwise within rtol 1e-4 / atol 2e-5; two calls
+    relative error <= 1e-5 and every element within 1e-5 of max|logit| (an
+    fp32 sum over H=7168 products carries rounding of that order in any
+    summation order; the CPU sgemm's and the tensor cores' differ); two calls
     give identical bits (split-K partials summed in a fixed order); the CUDA
     router fed these logits routes exactly like the oracle fed them."""
     sh = W.CONFIGS[cfg].replace(T=T)
@@ -88,7 +90,7 @@ def test_router_gemm_matches_fp32(cfg, T):
     err = _logits_err(got.cpu(), ref)
     print(f"{cfg} T={T}: router GEMM normwise rel err {err:.2e}")
     assert err <= 1e-5
-    torch.testing.assert_close(got.cpu(), ref, rtol=1e-4, atol=2e-5)
+    torch.testing.assert_close(got.cpu(), ref, rtol=1e-4, atol=1e-5 * float(ref.abs().max()))
     assert torch.equal(got, again)
     _check(got.cpu(), d["router_bias"], sh.n_group, sh.topk_group, sh.top_k)
 
@@ -101,4 +103,4 @@ def test_router_gemm_small_expert_count():
     got = gemms_b200.router_logits(x.cuda(), rw.cuda()).cpu()
     ref = R.router_logits(x, rw)
     assert _logits_err(got, ref) <= 1e-5
-    torch.testing.assert_close(got, ref, rtol=1e-4, atol=2e-5)
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5 * float(ref.abs().max()))
