@@ -373,6 +373,40 @@ def count_kernels_per_step(step_fn) -> int:
     return n
 
 
+def decode_sweep(d, kw, sh, hbm, Ts=(1, 8, 32, 128), steps=50, warmup=5):
+    """BASELINE config c2: the same full layer (same weights) on the first T
+    tokens, T in Ts, one GPU.  Decode streams the weights of every expert the
+    batch hits (+ the shared expert), so each line reports that weight traffic
+    per layer as HBM GB/s; the experts hit are counted from the batch's own
+    routing.  Every step reads >= 396 MB of weights (T=1: 8 experts + shared),
+    more than the 126 MB L2."""
+    import torch
+
+    import gemms_b200
+
+    args = (d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"])
+    res = {}
+    for T in Ts:
+        x = d["x"][:T].contiguous()
+        counts = gemms_b200.moe(x, *args, return_routing=True, **kw)[3]
+        hit = int((counts > 0).sum())
+        for _ in range(warmup):
+            gemms_b200.moe(x, *args, **kw)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            gemms_b200.moe(x, *args, **kw)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        nbytes = (hit + (1 if sh.shared else 0)) * sh.expert_bytes()
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[f"T={T}"] = {"ms_per_step": round(ms, 5), "tokens_per_s": round(T / (ms / 1e3), 1), "experts_hit": hit,
+                         "weight_bytes": nbytes, "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)}
+    return res
+
+
 def gpu_arm(a):
     if a.ep_combine:
         os.environ["GEMMS_EP_COMBINE"] = a.ep_combine
@@ -506,6 +540,10 @@ def gpu_arm(a):
                "d2h_bytes_per_step": outs[0].numel() * outs[0].element_size() * world,
                "path": "pinned host x -> gemms_b200.MoePipeline (public API; copies overlapped with the "
                        "layer on side streams) -> pinned host out, every step, every rank"}
+    decode = None
+    if group is None and cfg == "c1":
+        hbm_peak = _peaks()[0]
+        decode = decode_sweep(d, {k: v for k, v in kw.items() if k != "ep_group"}, sh, hbm_peak)
     clocks = sampler.stop() if sampler else None
 
     tokens_total = base.T
@@ -531,6 +569,12 @@ def gpu_arm(a):
                                    "best of 10 on this GPU"},
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
             "e2e": e2e, "clocks": clocks}
+    if decode is not None:
+        line["decode_c2"] = {"what": "BASELINE config c2 on the same GPU and weights: full layer (router GEMM, "
+                                     "routing, quantisation, grouped GEMMs, combine, shared expert) on the first T "
+                                     "tokens; GB/s = weight bytes of the experts hit (+ shared) per layer / time; "
+                                     "hbm_frac against the measured HBM copy bandwidth",
+                             **decode}
     if group is not None:
         # Dominant phase at N>1: the grouped GEMMs over the received rows
         # (GEMM1 + GEMM2 of the rank's E/N experts, all of them hit at c3).

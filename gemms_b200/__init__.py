@@ -10,12 +10,14 @@ Public operators (CUDA tensors only, no CPU fallback):
 * :func:`router_logits`, :func:`quantize_1x128` -- the router GEMM and the
   per-1x128 activation quantisation alone.
 * :class:`MoePipeline` -- host-to-host serving loop with PCIe copies overlapped.
+* ``torch.ops.gemms_b200.moe`` / ``torch.ops.gemms_b200.run`` -- the same layer
+  as PyTorch dispatcher operators (after :func:`load_torch_ops`).
 """
 from .ops import ShapeError, check_device_errors, moe, quantize_1x128, route, router_logits, run  # noqa: F401
-from ._lib import GemmsError, lib_path, load as load_library  # noqa: F401
+from ._lib import GemmsError, lib_path, load as load_library, load_torch_ops  # noqa: F401
 from . import workloads  # noqa: F401
 from .pipeline import MoePipeline  # noqa: F401
 
 __all__ = ["run", "moe", "route", "router_logits", "quantize_1x128", "ShapeError", "GemmsError", "check_device_errors",
-           "load_library", "lib_path", "workloads", "MoePipeline"]
+           "load_library", "load_torch_ops", "lib_path", "workloads", "MoePipeline"]
 __version__ = "0.1.0"

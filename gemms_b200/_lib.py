@@ -170,6 +170,28 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         return L
 
 
+_torch_ops_loaded = False
+
+
+def load_torch_ops(auto_build: bool = True) -> None:
+    """Registers ``torch.ops.gemms_b200.moe`` and ``torch.ops.gemms_b200.run``
+    (``gemms_b200/lib/libgemms_torch.so``, PyTorch dispatcher operators over
+    the same C ABI).  The C-ABI library is loaded first, so both share one
+    copy of it."""
+    global _torch_ops_loaded
+    if _torch_ops_loaded:
+        return
+    load(auto_build)
+    path = _build.TORCH_LIB
+    if not os.path.exists(path) and auto_build:
+        _build.build_torch_ops()
+    if not os.path.exists(path):
+        raise ImportError(f"gemms_b200 torch operator library missing: {path} (run `python -m gemms_b200.build`)")
+    import torch
+    torch.ops.load_library(path)
+    _torch_ops_loaded = True
+
+
 def strerror(code: int) -> str:
     try:
         return load(auto_build=False).gemms_strerror(code).decode()

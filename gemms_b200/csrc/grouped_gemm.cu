@@ -9,18 +9,17 @@
 // Design (one persistent CTA per SM, 384 threads, warp-specialised; the
 // control warpgroup 0-3 runs on 40-56 registers, the epilogue warpgroups on
 // 224-232 via setmaxnreg):
-//   warp 0      TMA producer: two 128-row weight boxes and the A tile(s)
-//               [128 rows x 128 B] per stage into a 2-4 deep smem ring.  GEMM1
-//               gathers its A rows straight from the token-major activations
-//               (each lane issues one tile::gather4 of four rows), so no
-//               per-expert copy of the activations is ever written; GEMM2
-//               loads the intermediate (already grouped) as tiles.
+//   warp 0      TMA producer: two 128-row weight boxes and (GEMM2) the A
+//               tiles [128 rows x 128 B] per stage into a 2-4 deep smem ring.
+//               GEMM1 gathers its A rows straight from the token-major
+//               activations (warps 2-3), so no per-expert copy of the
+//               activations is ever written; GEMM2 loads the intermediate
+//               (already grouped) as tiles.
 //   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
 //               (M=128, N=256, K=32 e4m3) from one thread; each 128-wide K
 //               block goes to one of two TMEM partial accumulators.
-//   warp 2      GEMM1 only: gathers the A rows (tile::gather4, four rows per
-//               lane) into the same stages.
-//   warp 3      idle (setmaxnreg works per warpgroup).
+//   warps 2-3   GEMM1: gather the A rows (16-byte cp.async per thread) into
+//               the same stages; GEMM2: idle (setmaxnreg works per warpgroup).
 //   warps 4-11  "promotion" epilogue: for every K block read the fp32 partial
 //               from TMEM, multiply by a_scale[row,kb] * w_scale[nblk,kb] and
 //               accumulate in registers (the block scales are arbitrary fp32,
@@ -97,6 +96,8 @@ struct GemmParams {
   // (nullptr: r itself); the scale of (source row q, K block kb) is
   // a_scale[kb * a_kb_stride + q * a_src_stride].
   const int32_t* a_src;
+  const uint8_t* a_rows;   // GEMM1: token-major e4m3 rows (gathered)
+  int a_row_stride;        // bytes between them
   const float* a_scale;
   int a_kb_stride;
   int a_src_stride;
@@ -153,13 +154,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* amax_x = reinterpret_cast<float*>(smem + C::kRingBytes + 512);  // [2 units][2 halves][128]
-  int* gidx = reinterpret_cast<int*>(smem + C::kRingBytes + 2560);       // GEMM1: [128] gather rows
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // GEMM1: the current tile's 128 source rows, one copy per gather warp (2, 3)
+  int* gidx_base = reinterpret_cast<int*>(smem + C::kRingBytes + 2560);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], MODE == 0 ? 2 : 1);  // GEMM1: weight producer + row-gather warp
+      mbar_init(&full[s], MODE == 0 ? 1 + 64 : 1);  // GEMM1: weight producer + 64 row-gather threads
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -191,30 +192,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kEpiFirstWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(Regs<MODE>::ctrl));
-   if (warp == 0 || (MODE == 0 && warp == 2)) {
+   if (warp == 0 || (MODE == 0 && warp >= 2)) {
     // ------------------------------------------------------------ producers
     // Warp 0, lane 0: waits for a free stage, arms the stage barrier with the
-    // bytes it loads and loads the two weight boxes (GEMM2 also its A tiles).
-    // GEMM1 only, warp 2: waits for the same stage, arms the barrier with the
-    // A tile's bytes and gathers the tile's 128 A rows, four per lane
-    // (tile::gather4).  Each stage barrier therefore expects one arrival per
-    // producer warp.  Both warps stop at the same K iteration under the test
-    // hook; a timeout stops either early (the drain below is bounded).
-    const bool gather = (MODE == 0 && warp == 2);
+    // bytes of its TMA loads and loads the two weight boxes (GEMM2 also its A
+    // tiles).  GEMM1 only, warps 2-3 (64 threads): gather the tile's 128 A
+    // rows from the token-major rows with 16-byte cp.async copies straight
+    // into the 128-byte-swizzled stage layout; thread t copies 16-byte chunk
+    // t % 8 of rows t / 8 + 8i (i < 16), so every warp instruction moves four
+    // whole 128-byte row segments.  Each gather thread's completion counts
+    // as one arrival on the stage barrier (expected: 1 + 64).  All producers
+    // stop at the same K iteration under the test hook; a timeout stops any
+    // of them early (the drains below are bounded).
+    const bool gather = (MODE == 0 && warp >= 2);
+    const int gt = (warp - 2) * 32 + lane;  // gather thread 0..63
+    const int gchunk = gt & 7, grow = gt >> 3;
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
       const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
       const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
       if (gather) {
-        // the tile's 128 source rows, staged once per unit; rows past the
-        // tile's count repeat its last row (loaded, never stored)
+        // the tile's 128 source rows, staged once per unit in this warp's own
+        // copy (no cross-warp barrier); rows past the tile's count repeat its
+        // last row (loaded, never stored)
         const int last = p.tile_rows[mt] - 1;
-        __syncwarp();  // previous unit's reads of gidx are done
+        int* gidx = gidx_base + (warp - 2) * 128;
+        __syncwarp();  // this warp is done with the previous unit's rows
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int rr = row0 + min(32 * j + lane, last);
-          gidx[32 * j + lane] = p.a_src ? __ldg(p.a_src + rr) : rr;
+          const int rr = row0 + min(lane + 32 * j, last);
+          gidx[lane + 32 * j] = p.a_src ? __ldg(p.a_src + rr) : rr;
         }
         __syncwarp();
       }
@@ -235,10 +243,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* st = smem + s * C::kStageBytes;
         if (gather) {
-          if (lane == 0) mbar_arrive_expect_tx(&full[s], kTileA);
-          __syncwarp();
-          const int4 src = *reinterpret_cast<const int4*>(gidx + 4 * lane);
-          tma_gather4(st + lane * 4 * BK, &tmA, &full[s], kb * BK, src.x, src.y, src.z, src.w, policy_evict_last());
+          const uint32_t dst = smem_u32(st) + grow * 128 + ((gchunk ^ grow) << 4);  // row grow + 8i: same XOR
+          const uint8_t* src = p.a_rows + (size_t)kb * BK + gchunk * 16;
+#pragma unroll 1
+          for (int i = 0; i < BM / 8; ++i)
+            cp_async_16(dst + i * 1024,
+                        src + (size_t)gidx_base[(warp - 2) * 128 + grow + 8 * i] * (uint32_t)p.a_row_stride);
+          cp_async_arrive_noinc(&full[s]);
         } else if (lane == 0) {
           const bool sh = (g == p.shared_group);
           const CUtensorMap* mb = sh ? &tmBs : &tmB;
@@ -258,7 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     // Let every copy this warp issued land before the CTA can exit.
-    if (lane == 0) {
+    if (gather) {
+      cp_async_wait_all();
+    } else if (lane == 0) {
       for (int s = 0; s < S && s < it; ++s) {
         const int last = s + S * ((it - 1 - s) / S);
         mbar_wait_drain(&full[s], (last / S) & 1);
@@ -294,6 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          // GEMM1's A rows arrived through cp.async (generic proxy); order
+          // them before this thread's MMAs read the stage (async proxy).
+          if (MODE == 0) fence_proxy_async_smem();
           if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait,
                          p.wait_limit)) {
             ok = false;
@@ -546,22 +562,6 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, ui
   return r == CUDA_SUCCESS ? GEMMS_OK : GEMMS_ERR_DRIVER;
 }
 
-// 2-D uint8 tensor [rows, inner] with a one-row, 128-byte box (128-byte
-// swizzle), for tile::gather4 row gathers.
-int make_gather_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride) {
-  auto fn = encode_fn();
-  if (!fn) return GEMMS_ERR_DRIVER;
-  if (!aligned16(base) || (row_stride % 16) || inner % BK) return GEMMS_ERR_ALIGN;
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {row_stride};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 1u};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? GEMMS_OK : GEMMS_ERR_DRIVER;
-}
-
 template <int MODE, int PLANES, int OUT_PLANES>
 int launch_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& bs, const GemmParams& p,
                   int max_units, cudaStream_t s) {
@@ -603,9 +603,10 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
   CUtensorMap ma, mb, mbs;
   int rc;
-  if (a.a_rows <= 0 || a.a_row_stride < a.H) return GEMMS_ERR_SHAPE;
-  if ((rc = make_gather_map(&ma, a.a, a.H, a.a_rows, a.a_row_stride))) return rc;
+  if (a.a_rows <= 0 || a.a_row_stride < a.H || a.a_row_stride > (1ll << 30)) return GEMMS_ERR_SHAPE;
+  if (!aligned16(a.a) || (a.a_row_stride % 16)) return GEMMS_ERR_ALIGN;  // 16-byte cp.async sources
   if ((rc = make_map(&mb, a.w13, a.H, (uint64_t)a.E_local * 2 * a.I, a.H))) return rc;
+  ma = mb;  // GEMM1 gathers A with cp.async: its A tensor map is unused
   if (a.sw13) {
     if ((rc = make_map(&mbs, a.sw13, a.H, 2ull * a.I, a.H))) return rc;
   } else {
@@ -625,6 +626,8 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.b_row_step = kBlock;
   p.b_row_hi = a.I;
   p.a_src = a.a_src;
+  p.a_rows = a.a;
+  p.a_row_stride = static_cast<int>(a.a_row_stride);
   p.a_scale = a.a_scale;
   p.a_kb_stride = static_cast<int>(a.a_scale_kb_stride);
   p.a_src_stride = static_cast<int>(a.a_scale_src_stride);

@@ -5,7 +5,7 @@
 // [H/128, T] scale (flashinfer_baseline.py:68-79) and gathers rows per expert
 // with index_select (:141-149).  Here the activations are quantised once,
 // token-major, in the reference's own layout; the grouped GEMM gathers each
-// expert's rows from them directly (tile::gather4), so no per-expert copy of
+// expert's rows from them directly (16-byte cp.async), so no per-expert copy of
 // the activations is written.
 #include "common.cuh"
 

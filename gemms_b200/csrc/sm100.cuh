@@ -123,18 +123,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Row gather: four rows (y0..y3) of a 2-D tensor whose tensor map has a box
-// one row high, columns [x, x + box width), into four consecutive box rows
-// at `dst` (same swizzle as a tiled load to that address), completing on
-// `bar`.  No multicast.  x * element size must be a multiple of 16 bytes.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y0,
-                                            int y1, int y2, int y3, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3),
-      "l"(policy)
-      : "memory");
+// 16-byte global -> shared copy (cp.async, bypassing L1).
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+
+// Arrive on `bar` once all prior cp.async copies of this thread have landed;
+// counts as one of the barrier's expected arrivals (.noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Orders shared-memory writes made through the generic proxy (cp.async,
+// st.shared) and observed by this thread before its later async-proxy
+// accesses (tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
