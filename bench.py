@@ -149,19 +149,19 @@ class ClockSampler:
 def algorithmic_bytes(sh, counts, planes: int, world: int = 1):
     """HBM bytes the two grouped GEMMs must move per launch (not counting
     re-reads): weights + scales of every expert that received rows (+ shared),
-    each token's quantised activation row once (GEMM1 gathers the rows of
-    every expert from the token-major copy), the SwiGLU intermediate (written
-    by GEMM1, read by GEMM2) and GEMM2's fp32 output accumulation."""
+    the grouped activation rows (one per routed pair, as GEMM1 reads them),
+    the SwiGLU intermediate (written by GEMM1, read by GEMM2) and GEMM2's fp32
+    output accumulation."""
     H, I = sh.H, sh.I
     hit = int((counts > 0).sum())
     rows = int(counts.sum()) + (sh.T if sh.shared else 0)
     n_exp = hit + (1 if sh.shared else 0)
     w13 = 2 * I * H + 4 * (2 * I // 128) * (H // 128)
     w2 = H * I + 4 * (H // 128) * (I // 128)
-    x_rows = sh.T * (H + 4 * H // 128)
+    a_rows = rows * (H + 4 * H // 128)
     inter = rows * (planes * I + 4 * I // 128)
     out_acc = sh.T * H * 4 * 2  # fp32 accumulation target, read+write once
-    g1 = n_exp * w13 + x_rows + inter
+    g1 = n_exp * w13 + a_rows + inter
     g2 = n_exp * w2 + inter + out_acc
     return {"gemm1": g1, "gemm2": g2, "experts_hit": hit, "rows": rows}
 
@@ -579,16 +579,15 @@ def gpu_arm(a):
         # Dominant phase at N>1: the grouped GEMMs over the received rows
         # (GEMM1 + GEMM2 of the rank's E/N experts, all of them hit at c3).
         # same model as algorithmic_bytes: weights (+ scales) of the local
-        # experts hit (+ shared), each received row once (GEMM1 gathers it for
-        # every local expert it names), the intermediate (one per grouped row)
-        # written and read, the fp32 result rows (received rows; the shared
-        # expert's T rows) read and written
+        # experts hit (+ shared), the grouped rows (one per received row and
+        # local expert), the intermediate written and read, the fp32 result
+        # rows (received rows; the shared expert's T rows) read and written
         H, I = sh.H, sh.I
         w_exp = 3 * I * H + 4 * (2 * I // 128) * (H // 128) + 4 * (H // 128) * (I // 128)
         row_b = H + 4 * H // 128
         inter_b = 2 * (planes * I + 4 * I // 128)
         R, P = ep_timeline["recv_rows"], ep_timeline["pair_rows"]
-        ffn_bytes = (ep_timeline["experts_hit"] * w_exp + R * row_b + P * inter_b + R * H * 4 * 2
+        ffn_bytes = (ep_timeline["experts_hit"] * w_exp + P * (row_b + inter_b) + R * H * 4 * 2
                      + ((w_exp + sh.T * (row_b + inter_b) + sh.T * H * 4 * 2) if sh.shared else 0))
         ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) + ep_timeline.get("shared_ffn_2", 0.0)
                                               if sh.shared else 0.0)

@@ -78,10 +78,29 @@ struct AssignArgs {
   const int32_t* offsets;
   int32_t* row_token;     // [rows]
   float* row_weight;      // [rows]
-  int32_t* pair_row;      // optional [T, top_k]: grouped row of each (token, k) pair
+  int32_t* pair_row;      // [T, top_k]
   int shared_rows;        // >0: rows offsets[E_local] + t get token t, weight 1
 };
 int launch_assign(const AssignArgs& a, cudaStream_t s);
+
+// Gather (and for bf16 input, quantise per 1x128) activation rows into the
+// expert-grouped operand: rows_fp8 [R, H], rows_scale [H/128, ld].
+struct PermuteArgs {
+  int mode;                        // GEMMS_INPUT_BF16 / GEMMS_INPUT_FP8
+  const __nv_bfloat16* x_bf16;     // [T, H]
+  const uint8_t* x_fp8;            // [T, H]
+  const float* x_scale;            // [H/128, T] (or strided, see below)
+  int T, H, top_k;
+  long long x_row_stride;          // bytes between fp8 input rows (0: H)
+  long long scale_kb_stride;       // floats between 128-column blocks of x_scale (0: T)
+  long long scale_t_stride;        // floats between tokens of x_scale (0: 1)
+  const int32_t* pair_row;         // [T, top_k] (-1 = not local)
+  const int32_t* shared_row0;      // device int (nullptr: none); token t also goes to row *shared_row0 + t
+  uint8_t* rows_fp8;
+  float* rows_scale;
+  int scale_ld;
+};
+int launch_permute(const PermuteArgs& a, cudaStream_t s);
 
 // Token-major per-1x128 quantisation: bf16 [T, H] -> e4m3 [T, H] + fp32 scale [H/128, T].
 int launch_quantize(const __nv_bfloat16* x, int T, int H, uint8_t* xq, float* xq_scale, cudaStream_t s);
@@ -101,13 +120,7 @@ struct GemmGroupsArgs {
 
 struct Gemm1Args {
   GemmGroupsArgs g;
-  // A rows are gathered: grouped row r reads source row a_src[r] (nullptr:
-  // r) of the e4m3 rows at `a` (a_rows rows of H bytes, a_row_stride bytes
-  // apart); its scale for K block kb is
-  // a_scale[kb * a_scale_kb_stride + source * a_scale_src_stride].
-  const uint8_t* a; int a_rows; long long a_row_stride;
-  const int32_t* a_src;
-  const float* a_scale; long long a_scale_kb_stride; long long a_scale_src_stride;
+  const uint8_t* a;  int a_rows;  const float* a_scale; int a_scale_ld;    // [R, H], [H/128, ld]
   const uint8_t* w13; const float* w13_scale; int E_local;                 // [E_local, 2I, H]
   const uint8_t* sw13; const float* sw13_scale;                            // shared [2I, H]
   int H, I;

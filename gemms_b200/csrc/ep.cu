@@ -174,13 +174,15 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
   }
 }
 
-// Thread per received row: local-expert histogram.
+// Thread per received row: local-expert histogram and pair_row = -1.
 __global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R, int H, int top_k,
-                               int local_offset, int E_local, int32_t* __restrict__ counts, int* err) {
+                               int local_offset, int E_local, int32_t* __restrict__ counts,
+                               int32_t* __restrict__ pair_row, int* err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= R) return;
   const int32_t* ids = reinterpret_cast<const int32_t*>(recv + (size_t)r * row_bytes + H + 4 * (H / kBlock));
   for (int j = 0; j < top_k; ++j) {
+    pair_row[(size_t)r * top_k + j] = -1;
     const int e = ids[j];
     if (e < 0) continue;
     const int le = e - local_offset;
@@ -269,8 +271,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
 
 struct EpFfnLayout {
   int groups, max_tiles, scale_ld;
-  size_t err, counts, offsets, tile_group, tile_row0, tile_rows, num_tiles, row_token, row_weight;
-  size_t inter, inter_scale, total, head;
+  size_t err, counts, offsets, tile_group, tile_row0, tile_rows, num_tiles, pair_row, row_token, row_weight;
+  size_t a_rows, a_scale, inter, inter_scale, total, head;
 };
 
 EpFfnLayout ep_ffn_layout(int R_max, int H, int I, int E_local, int top_k, int planes) {
@@ -293,8 +295,11 @@ EpFfnLayout ep_ffn_layout(int R_max, int H, int I, int E_local, int top_k, int p
   L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
   L.tile_rows = take(sizeof(int32_t) * L.max_tiles);
   L.num_tiles = take(sizeof(int32_t));
+  L.pair_row = take(sizeof(int32_t) * (size_t)std::max(R_max, 1) * top_k);
   L.row_token = take(sizeof(int32_t) * P);
   L.row_weight = take(sizeof(float) * P);
+  L.a_rows = take((size_t)P * H);
+  L.a_scale = take(sizeof(float) * (size_t)(H / kBlock) * L.scale_ld);
   L.inter = take((size_t)P * planes * I);
   L.inter_scale = take(sizeof(float) * (size_t)(I / kBlock) * L.scale_ld);
   L.total = o;
@@ -366,8 +371,9 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   const uint8_t* recv = static_cast<const uint8_t*>(recv_buf);
   GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, L.head, st));
   GEMMS_CUDA_TRY(cudaMemsetAsync(out_rows, 0, sizeof(float) * (size_t)R * H, st));
+  int32_t* pair_row = at<int32_t>(ws, L.pair_row);
   ep_hist_kernel<<<cdiv(R, 256), 256, 0, st>>>(recv, rb, R, H, top_k, local_expert_offset, E_local,
-                                                at<int32_t>(ws, L.counts), err);
+                                                at<int32_t>(ws, L.counts), pair_row, err);
   GEMMS_CUDA_TRY(cudaGetLastError());
   int rc;
   PlanArgs pa{};
@@ -395,9 +401,26 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   sa.offsets = pa.offsets;
   sa.row_token = at<int32_t>(ws, L.row_token);
   sa.row_weight = at<float>(ws, L.row_weight);
-  sa.pair_row = nullptr;
+  sa.pair_row = pair_row;
   sa.shared_rows = 0;
   if ((rc = launch_assign(sa, st))) return rc;
+
+  PermuteArgs qa{};
+  qa.mode = GEMMS_INPUT_FP8;
+  qa.x_fp8 = recv;
+  qa.x_scale = reinterpret_cast<const float*>(recv + H);
+  qa.x_row_stride = static_cast<long long>(rb);
+  qa.scale_kb_stride = 1;
+  qa.scale_t_stride = static_cast<long long>(rb / 4);
+  qa.T = R;
+  qa.H = H;
+  qa.top_k = top_k;
+  qa.pair_row = pair_row;
+  qa.shared_row0 = nullptr;
+  qa.rows_fp8 = at<uint8_t>(ws, L.a_rows);
+  qa.rows_scale = at<float>(ws, L.a_scale);
+  qa.scale_ld = L.scale_ld;
+  if ((rc = launch_permute(qa, st))) return rc;
 
   GemmGroupsArgs gg{};
   gg.tile_group = pa.tile_group;
@@ -410,15 +433,10 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
 
   Gemm1Args g1{};
   g1.g = gg;
-  // GEMM1 gathers each pair row's activations from the received packed row
-  // (e4m3 [H] then fp32 scales [H/128]) in place.
-  g1.a = recv;
-  g1.a_rows = R;
-  g1.a_row_stride = static_cast<long long>(rb);
-  g1.a_src = sa.row_token;  // pair row -> received row
-  g1.a_scale = reinterpret_cast<const float*>(recv + H);
-  g1.a_scale_kb_stride = 1;
-  g1.a_scale_src_stride = static_cast<long long>(rb / 4);
+  g1.a = qa.rows_fp8;
+  g1.a_rows = P;
+  g1.a_scale = qa.rows_scale;
+  g1.a_scale_ld = L.scale_ld;
   g1.w13 = static_cast<const uint8_t*>(w13);
   g1.w13_scale = w13_scale;
   g1.E_local = E_local;

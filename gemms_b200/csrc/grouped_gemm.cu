@@ -9,17 +9,12 @@
 // Design (one persistent CTA per SM, 384 threads, warp-specialised; the
 // control warpgroup 0-3 runs on 40-56 registers, the epilogue warpgroups on
 // 224-232 via setmaxnreg):
-//   warp 0      TMA producer: two 128-row weight boxes and (GEMM2) the A
-//               tiles [128 rows x 128 B] per stage into a 2-4 deep smem ring.
-//               GEMM1 gathers its A rows straight from the token-major
-//               activations (warps 2-3), so no per-expert copy of the
-//               activations is ever written; GEMM2 loads the intermediate
-//               (already grouped) as tiles.
+//   warp 0      TMA producer: A tile(s) [128 rows x 128 B] per plane and two
+//               128-row weight boxes per stage into a 2-4 deep smem ring.
 //   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
 //               (M=128, N=256, K=32 e4m3) from one thread; each 128-wide K
 //               block goes to one of two TMEM partial accumulators.
-//   warps 2-3   GEMM1: gather the A rows (16-byte cp.async per thread) into
-//               the same stages; GEMM2: idle (setmaxnreg works per warpgroup).
+//   warps 2-3   idle (setmaxnreg works per warpgroup).
 //   warps 4-11  "promotion" epilogue: for every K block read the fp32 partial
 //               from TMEM, multiply by a_scale[row,kb] * w_scale[nblk,kb] and
 //               accumulate in registers (the block scales are arbitrary fp32,
@@ -92,15 +87,9 @@ struct GemmParams {
   int w_rows;        // weight rows per expert
   int b_row_step;    // weight rows per N tile step
   int b_row_hi;      // row offset of the second 128-row weight box
-  // A operand rows: GEMM1 gathers source row a_src[r] for grouped row r
-  // (nullptr: r itself); the scale of (source row q, K block kb) is
-  // a_scale[kb * a_kb_stride + q * a_src_stride].
-  const int32_t* a_src;
-  const uint8_t* a_rows;   // GEMM1: token-major e4m3 rows (gathered)
-  int a_row_stride;        // bytes between them
+  int prefetch;      // weight K-blocks prefetched into L2 ahead of the smem ring
   const float* a_scale;
-  int a_kb_stride;
-  int a_src_stride;
+  int a_scale_ld;
   const float* w_scale;   // [E, w_rows/128, kb_count]
   const float* sw_scale;  // [w_rows/128, kb_count]
   // GEMM1 epilogue
@@ -154,13 +143,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* amax_x = reinterpret_cast<float*>(smem + C::kRingBytes + 512);  // [2 units][2 halves][128]
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // GEMM1: the current tile's 128 source rows, one copy per gather warp (2, 3)
-  int* gidx_base = reinterpret_cast<int*>(smem + C::kRingBytes + 2560);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], MODE == 0 ? 1 + 64 : 1);  // GEMM1: weight producer + 64 row-gather threads
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -192,86 +180,70 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kEpiFirstWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(Regs<MODE>::ctrl));
-   if (warp == 0 || (MODE == 0 && warp >= 2)) {
-    // ------------------------------------------------------------ producers
-    // Warp 0, lane 0: waits for a free stage, arms the stage barrier with the
-    // bytes of its TMA loads and loads the two weight boxes (GEMM2 also its A
-    // tiles).  GEMM1 only, warps 2-3 (64 threads): gather the tile's 128 A
-    // rows from the token-major rows with 16-byte cp.async copies straight
-    // into the 128-byte-swizzled stage layout; thread t copies 16-byte chunk
-    // t % 8 of rows t / 8 + 8i (i < 16), so every warp instruction moves four
-    // whole 128-byte row segments.  Each gather thread's completion counts
-    // as one arrival on the stage barrier (expected: 1 + 64).  All producers
-    // stop at the same K iteration under the test hook; a timeout stops any
-    // of them early (the drains below are bounded).
-    const bool gather = (MODE == 0 && warp >= 2);
-    const int gt = (warp - 2) * 32 + lane;  // gather thread 0..63
-    const int gchunk = gt & 7, grow = gt >> 3;
-    int it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-      const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
-      const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
-      if (gather) {
-        // the tile's 128 source rows, staged once per unit in this warp's own
-        // copy (no cross-warp barrier); rows past the tile's count repeat its
-        // last row (loaded, never stored)
-        const int last = p.tile_rows[mt] - 1;
-        int* gidx = gidx_base + (warp - 2) * 128;
-        __syncwarp();  // this warp is done with the previous unit's rows
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int rr = row0 + min(lane + 32 * j, last);
-          gidx[lane + 32 * j] = p.a_src ? __ldg(p.a_src + rr) : rr;
-        }
-        __syncwarp();
+   if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      // Weight coordinates of this CTA's it-th K iteration (units are strided
+      // by gridDim.x); used both to load and to prefetch ahead into L2.
+      const int my_units = total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+      const int my_iters = my_units * p.kb_count;
+      auto weight_rows = [&](int it, int& kb, int& wrow, const CUtensorMap*& mb) {
+        const int i = it / p.kb_count;
+        kb = it - i * p.kb_count;
+        const int u = blockIdx.x + i * gridDim.x;
+        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        const int g = p.tile_group[mt];
+        const bool sh = (g == p.shared_group);
+        mb = sh ? &tmBs : &tmB;
+        wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
+      };
+      for (int pf = 0; pf < p.prefetch && pf < my_iters; ++pf) {
+        int kb, wrow;
+        const CUtensorMap* mb;
+        weight_rows(pf, kb, wrow, mb);
+        tma_prefetch_l2_2d(mb, kb * BK, wrow, pol_w);
+        tma_prefetch_l2_2d(mb, kb * BK, wrow + p.b_row_hi, pol_w);
       }
-      for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
-        const int s = it % S;
-        const uint32_t round = it / S;
-        int go = 1;
-        if (lane == 0) {
-          if (blockIdx.x == 0 && it == p.stall_iter)
-            go = 0;  // test hook: withhold this stage (no expect_tx, no loads)
-          else
-            go = mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait, p.wait_limit);
-        }
-        go = __shfl_sync(0xffffffffu, go, 0);
-        if (!go) {
-          ok = false;
-          break;
-        }
-        uint8_t* st = smem + s * C::kStageBytes;
-        if (gather) {
-          const uint32_t dst = smem_u32(st) + grow * 128 + ((gchunk ^ grow) << 4);  // row grow + 8i: same XOR
-          const uint8_t* src = p.a_rows + (size_t)kb * BK + gchunk * 16;
-#pragma unroll 1
-          for (int i = 0; i < BM / 8; ++i)
-            cp_async_16(dst + i * 1024,
-                        src + (size_t)gidx_base[(warp - 2) * 128 + grow + 8 * i] * (uint32_t)p.a_row_stride);
-          cp_async_arrive_noinc(&full[s]);
-        } else if (lane == 0) {
-          const bool sh = (g == p.shared_group);
-          const CUtensorMap* mb = sh ? &tmBs : &tmB;
-          const int wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
-          mbar_arrive_expect_tx(&full[s], C::kStageBytes - (MODE == 0 ? kTileA : 0));
-          if (MODE != 0) {
-            const uint64_t pol_a = policy_evict_last();
-#pragma unroll
-            for (int pl = 0; pl < PLANES; ++pl)
-              tma_load_2d(st + pl * kTileA, &tmA, &full[s], pl * p.plane_stride + kb * BK, row0, pol_a);
+      int it = 0;
+      for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
+        const bool sh = (g == p.shared_group);
+        const CUtensorMap* mb = sh ? &tmBs : &tmB;
+        const int wrow = (sh ? 0 : g * p.w_rows) + nt * p.b_row_step;
+        bool ok = true;
+        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (p.prefetch > 0 && it + p.prefetch < my_iters) {
+            int pkb, pwrow;
+            const CUtensorMap* pmb;
+            weight_rows(it + p.prefetch, pkb, pwrow, pmb);
+            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow, pol_w);
+            tma_prefetch_l2_2d(pmb, pkb * BK, pwrow + p.b_row_hi, pol_w);
           }
-          const uint64_t pol_w = policy_evict_first();
+          if (blockIdx.x == 0 && it == p.stall_iter) {
+            ok = false;  // test hook: withhold this stage (no expect_tx, no loads)
+            break;
+          }
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, p.err, kErrGemmProducerWait, p.wait_limit)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+#pragma unroll
+          for (int pl = 0; pl < PLANES; ++pl)
+            tma_load_2d(st + pl * kTileA, &tmA, &full[s], pl * p.plane_stride + kb * BK, row0, pol_a);
           uint8_t* sb = st + PLANES * kTileA;
           tma_load_2d(sb, mb, &full[s], kb * BK, wrow, pol_w);
           tma_load_2d(sb + kTileA, mb, &full[s], kb * BK, wrow + p.b_row_hi, pol_w);
         }
+        if (!ok) break;
       }
-    }
-    // Let every copy this warp issued land before the CTA can exit.
-    if (gather) {
-      cp_async_wait_all();
-    } else if (lane == 0) {
+      // Let every copy this thread issued land before the CTA can exit.
       for (int s = 0; s < S && s < it; ++s) {
         const int last = s + S * ((it - 1 - s) / S);
         mbar_wait_drain(&full[s], (last / S) & 1);
@@ -307,9 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          // GEMM1's A rows arrived through cp.async (generic proxy); order
-          // them before this thread's MMAs read the stage (async proxy).
-          if (MODE == 0) fence_proxy_async_smem();
           if (!mbar_wait(&pempty[buf], ((acc_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrGemmMmaWait,
                          p.wait_limit)) {
             ok = false;
@@ -370,9 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Scales are prefetched three K blocks ahead (global-load latency is
       // ~1 pipeline iteration under load).  Rows past the tile's valid count
       // read row 0's scale and are never stored.
-      const int arow = row0 + (valid ? r : 0);
-      const int asrc = (MODE == 0 && p.a_src) ? __ldg(p.a_src + arow) : arow;
-      const float* a_sc = p.a_scale + (size_t)asrc * p.a_src_stride;
+      const float* a_sc = p.a_scale + row0 + (valid ? r : 0);
       const float* w0p = ws + (size_t)blk0 * p.kb_count;
       const float* w1p = ws + (size_t)blk1 * p.kb_count;
       float acc[128];
@@ -382,12 +349,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       float as0 = __ldg(a_sc), w00 = __ldg(w0p), w10 = __ldg(w1p);
       float as1 = 0.f, w01 = 0.f, w11 = 0.f, as2 = 0.f, w02 = 0.f, w12 = 0.f;
       if (KB > 1) {
-        as1 = __ldg(a_sc + (size_t)p.a_kb_stride);
+        as1 = __ldg(a_sc + (size_t)p.a_scale_ld);
         w01 = __ldg(w0p + 1);
         w11 = __ldg(w1p + 1);
       }
       if (KB > 2) {
-        as2 = __ldg(a_sc + 2 * (size_t)p.a_kb_stride);
+        as2 = __ldg(a_sc + 2 * (size_t)p.a_scale_ld);
         w02 = __ldg(w0p + 2);
         w12 = __ldg(w1p + 2);
       }
@@ -396,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         as0 = as1; w00 = w01; w10 = w11;
         as1 = as2; w01 = w02; w11 = w12;
         if (kb + 3 < KB) {
-          as2 = __ldg(a_sc + (size_t)(kb + 3) * p.a_kb_stride);
+          as2 = __ldg(a_sc + (size_t)(kb + 3) * p.a_scale_ld);
           w02 = __ldg(w0p + kb + 3);
           w12 = __ldg(w1p + kb + 3);
         }
@@ -430,15 +397,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(lane_base + buf * BN + col0, v0);
           tmem_ld_32x32b_x32(lane_base + buf * BN + col1, v1);
           tmem_ld_wait();
+          if (c == 2) {
+            // The buffer's last columns are in registers: release it to the
+            // MMA before this round's FMAs (shortens the MMA -> promotion ->
+            // MMA hand-off by the FMA time).
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pempty[buf]);
+          }
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             ffma2(acc[32 * c + i], acc[32 * c + i + 1], fa, v0[i], v0[i + 1]);
             ffma2(acc[32 * c + 32 + i], acc[32 * c + 33 + i], fb, v1[i], v1[i + 1]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[buf]);
       }
       if (!ok) break;
 
@@ -547,6 +519,20 @@ void apply_wait_knobs(GemmParams& p, int gemm) {
                                                                         : -1;
 }
 
+// Weight K-blocks a CTA keeps in flight toward L2 beyond its smem ring.  The
+// weight stream is DRAM-latency bound (one 32 KB stage per K-block per SM);
+// GEMMS_PREFETCH overrides the default for tuning.
+int prefetch_depth() {
+  static int depth = -1;
+  if (depth < 0) {
+    const char* e = getenv("GEMMS_PREFETCH");
+    depth = e ? atoi(e) : 0;
+    if (depth < 0) depth = 0;
+    if (depth > 64) depth = 64;
+  }
+  return depth;
+}
+
 // 2-D uint8 tensor [rows, inner] with a 128x128 box and 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride) {
   auto fn = encode_fn();
@@ -603,10 +589,8 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   if (a.planes < 2 || a.planes > 3) return GEMMS_ERR_SHAPE;
   CUtensorMap ma, mb, mbs;
   int rc;
-  if (a.a_rows <= 0 || a.a_row_stride < a.H || a.a_row_stride > (1ll << 30)) return GEMMS_ERR_SHAPE;
-  if (!aligned16(a.a) || (a.a_row_stride % 16)) return GEMMS_ERR_ALIGN;  // 16-byte cp.async sources
+  if ((rc = make_map(&ma, a.a, a.H, a.a_rows, a.H))) return rc;
   if ((rc = make_map(&mb, a.w13, a.H, (uint64_t)a.E_local * 2 * a.I, a.H))) return rc;
-  ma = mb;  // GEMM1 gathers A with cp.async: its A tensor map is unused
   if (a.sw13) {
     if ((rc = make_map(&mbs, a.sw13, a.H, 2ull * a.I, a.H))) return rc;
   } else {
@@ -625,12 +609,9 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.w_rows = 2 * a.I;
   p.b_row_step = kBlock;
   p.b_row_hi = a.I;
-  p.a_src = a.a_src;
-  p.a_rows = a.a;
-  p.a_row_stride = static_cast<int>(a.a_row_stride);
+  p.prefetch = prefetch_depth();
   p.a_scale = a.a_scale;
-  p.a_kb_stride = static_cast<int>(a.a_scale_kb_stride);
-  p.a_src_stride = static_cast<int>(a.a_scale_src_stride);
+  p.a_scale_ld = a.a_scale_ld;
   p.w_scale = a.w13_scale;
   p.sw_scale = a.sw13_scale;
   p.inter = a.inter;
@@ -670,10 +651,9 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.w_rows = a.H;
   p.b_row_step = BN;
   p.b_row_hi = kBlock;
-  p.a_src = nullptr;
+  p.prefetch = prefetch_depth();
   p.a_scale = a.inter_scale;
-  p.a_kb_stride = a.inter_scale_ld;
-  p.a_src_stride = 1;
+  p.a_scale_ld = a.inter_scale_ld;
   p.w_scale = a.w2_scale;
   p.sw_scale = a.sw2_scale;
   p.row_dest = a.row_dest;

@@ -15,8 +15,8 @@ namespace {
 struct FwdLayout {
   int T, K, H, I, E_loc, shared, planes;
   int R_max, groups, max_tiles, scale_ld;
-  size_t err, counts, topk_idx, topk_w, offsets, tile_group, tile_row0, tile_rows, num_tiles;
-  size_t row_token, row_weight, xq, xq_scale, inter, inter_scale, out_acc, total;
+  size_t err, counts, topk_idx, topk_w, pair_row, offsets, tile_group, tile_row0, tile_rows, num_tiles;
+  size_t row_token, row_weight, a_rows, a_scale, inter, inter_scale, out_acc, total;
   RouterPlan router;
   size_t router_planes, router_partials;  // router GEMM scratch (GEMMS_INPUT_BF16 only)
   size_t head_bytes;  // [0, head_bytes) is zeroed each call (error word + counts)
@@ -46,6 +46,7 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.head_bytes = o;
   L.topk_idx = take(sizeof(int32_t) * (size_t)L.T * L.K);
   L.topk_w = take(sizeof(float) * (size_t)L.T * L.K);
+  L.pair_row = take(sizeof(int32_t) * (size_t)L.T * L.K);
   L.offsets = take(sizeof(int32_t) * (L.groups + 1));
   L.tile_group = take(sizeof(int32_t) * L.max_tiles);
   L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
@@ -53,10 +54,8 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.num_tiles = take(sizeof(int32_t));
   L.row_token = take(sizeof(int32_t) * (size_t)std::max(L.R_max, 1));
   L.row_weight = take(sizeof(float) * (size_t)std::max(L.R_max, 1));
-  if (s.input_mode == GEMMS_INPUT_BF16) {  // token-major quantised activations (GEMM1 gathers from them)
-    L.xq = take((size_t)std::max(L.T, 1) * L.H);
-    L.xq_scale = take(sizeof(float) * (size_t)(L.H / kBlock) * std::max(L.T, 1));
-  }
+  L.a_rows = take((size_t)std::max(L.R_max, 1) * L.H);
+  L.a_scale = take(sizeof(float) * (size_t)(L.H / kBlock) * L.scale_ld);
   L.inter = take((size_t)std::max(L.R_max, 1) * L.planes * L.I);
   L.inter_scale = take(sizeof(float) * (size_t)(L.I / kBlock) * L.scale_ld);
   L.out_acc = take(sizeof(float) * (size_t)L.T * L.H);
@@ -196,7 +195,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   ra.topk_idx = at<int32_t>(ws, L.topk_idx);
   ra.topk_w = at<float>(ws, L.topk_w);
   ra.counts = at<int32_t>(ws, L.counts);
-  ra.pair_row = nullptr;
+  ra.pair_row = at<int32_t>(ws, L.pair_row);
   if ((rc = launch_route(ra, st))) return rc;
 
   PlanArgs pa{};
@@ -222,24 +221,24 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   sa.offsets = pa.offsets;
   sa.row_token = at<int32_t>(ws, L.row_token);
   sa.row_weight = at<float>(ws, L.row_weight);
-  sa.pair_row = nullptr;
+  sa.pair_row = ra.pair_row;
   sa.shared_rows = pa.shared_rows;
   if ((rc = launch_assign(sa, st))) return rc;
 
-  // Token-major e4m3 activations + [H/128, T] scales: quantised here from
-  // bf16, or the caller's (run()'s hidden_states / hidden_states_scale).
-  const uint8_t* xq;
-  const float* xq_scale;
-  if (s.input_mode == GEMMS_INPUT_BF16) {
-    xq = at<uint8_t>(ws, L.xq);
-    xq_scale = at<float>(ws, L.xq_scale);
-    if ((rc = launch_quantize(static_cast<const __nv_bfloat16*>(args->hidden_bf16), s.T, s.H,
-                              at<uint8_t>(ws, L.xq), at<float>(ws, L.xq_scale), st)))
-      return rc;
-  } else {
-    xq = static_cast<const uint8_t*>(args->hidden_fp8);
-    xq_scale = args->hidden_scale;
-  }
+  PermuteArgs qa{};
+  qa.mode = s.input_mode;
+  qa.x_bf16 = static_cast<const __nv_bfloat16*>(args->hidden_bf16);
+  qa.x_fp8 = static_cast<const uint8_t*>(args->hidden_fp8);
+  qa.x_scale = args->hidden_scale;
+  qa.T = s.T;
+  qa.H = s.H;
+  qa.top_k = s.top_k;
+  qa.pair_row = ra.pair_row;
+  qa.shared_row0 = L.shared ? pa.offsets + s.E_local : nullptr;
+  qa.rows_fp8 = at<uint8_t>(ws, L.a_rows);
+  qa.rows_scale = at<float>(ws, L.a_scale);
+  qa.scale_ld = L.scale_ld;
+  if ((rc = launch_permute(qa, st))) return rc;
 
   GemmGroupsArgs gg{};
   gg.tile_group = pa.tile_group;
@@ -251,13 +250,10 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
 
   Gemm1Args g1{};
   g1.g = gg;
-  g1.a = xq;
-  g1.a_rows = s.T;
-  g1.a_row_stride = s.H;
-  g1.a_src = sa.row_token;  // grouped row -> token
-  g1.a_scale = xq_scale;
-  g1.a_scale_kb_stride = s.T;
-  g1.a_scale_src_stride = 1;
+  g1.a = qa.rows_fp8;
+  g1.a_rows = L.R_max;
+  g1.a_scale = qa.rows_scale;
+  g1.a_scale_ld = L.scale_ld;
   g1.w13 = static_cast<const uint8_t*>(args->w13);
   g1.w13_scale = args->w13_scale;
   g1.E_local = std::max(s.E_local, 1);
@@ -452,11 +448,8 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
   g1.g = gg;
   g1.a = static_cast<const uint8_t*>(rows_fp8);
   g1.a_rows = R_max;
-  g1.a_row_stride = H;
-  g1.a_src = nullptr;  // rows are already grouped
   g1.a_scale = rows_scale;
-  g1.a_scale_kb_stride = R_max;
-  g1.a_scale_src_stride = 1;
+  g1.a_scale_ld = R_max;
   g1.w13 = static_cast<const uint8_t*>(w13);
   g1.w13_scale = w13_scale;
   g1.E_local = E_local;

@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
       const int r = base + warp_excl + __popc(ballot & ((1u << lane) - 1u));
       a.row_token[r] = t;
       a.row_weight[r] = a.topk_w[(size_t)t * stride + jsel];
-      if (a.pair_row) a.pair_row[(size_t)t * a.top_k + jsel] = r;
+      a.pair_row[(size_t)t * a.top_k + jsel] = r;
     }
     __syncthreads();
     if (tid == 0) s_base = base + s_warp[nwarps - 1];

@@ -123,24 +123,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// 16-byte global -> shared copy (cp.async, bypassing L1).
-__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
-}
-
-// Arrive on `bar` once all prior cp.async copies of this thread have landed;
-// counts as one of the barrier's expected arrivals (.noinc).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-// Orders shared-memory writes made through the generic proxy (cp.async,
-// st.shared) and observed by this thread before its later async-proxy
-// accesses (tcgen05.mma operand reads).
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// Prefetch a 2-D tile into L2 (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "l"(policy)
+      : "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
