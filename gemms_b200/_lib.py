@@ -136,9 +136,10 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_ep_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
         L.gemms_ep_dispatch.restype = c_int32
-        L.gemms_ep_ffn_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]
+        L.gemms_ep_ffn_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]
         L.gemms_ep_ffn_workspace_size.restype = c_size_t
         L.gemms_ep_expert_ffn.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                          c_int32,
                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                           c_void_p]
         L.gemms_ep_expert_ffn.restype = c_int32

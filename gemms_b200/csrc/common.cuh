@@ -65,6 +65,7 @@ struct PlanArgs {
   int32_t* tile_rows;
   int32_t* num_tiles;     // [1]
   int max_tiles;
+  int row_capacity;       // grouped rows the buffers hold: more rows -> error word, no tiles
   int* err;
 };
 int launch_plan(const PlanArgs& a, cudaStream_t s);
@@ -79,7 +80,8 @@ struct AssignArgs {
   int32_t* row_token;     // [rows]
   float* row_weight;      // [rows]
   int32_t* pair_row;      // [T, top_k]
-  int shared_rows;        // >0: rows offsets[E_local] + t get token t, weight 1
+  int shared_rows;
+  int row_capacity;       // rows at or past it are not written (plan_kernel reports the overflow)        // >0: rows offsets[E_local] + t get token t, weight 1
 };
 int launch_assign(const AssignArgs& a, cudaStream_t s);
 

@@ -58,17 +58,22 @@ __device__ __forceinline__ unsigned dest_mask(const int32_t* idx, int top_k, int
   return m;
 }
 
-// Thread per token: per-destination row counts.
-__global__ void ep_count_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k, int E_local,
+// Thread per token: per-destination row counts (send_counts[0][d]) and
+// routed (token, expert) pairs (send_counts[1][d]), which size the
+// destination's grouped rows exactly.
+__global__ void ep_count_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k, int E_local, int world,
                                 int32_t* __restrict__ send_counts) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
-  unsigned m = dest_mask(topk_idx + (size_t)t * top_k, top_k, E_local);
+  const int32_t* idx = topk_idx + (size_t)t * top_k;
+  unsigned m = dest_mask(idx, top_k, E_local);
   while (m) {
     const int d = __ffs(m) - 1;
     m &= m - 1;
     atomicAdd(send_counts + d, 1);
   }
+  for (int j = 0; j < top_k; ++j)
+    if (idx[j] >= 0) atomicAdd(send_counts + world + idx[j] / E_local, 1);
 }
 
 // Block per destination: send rows in increasing token order.
@@ -270,14 +275,16 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
 }
 
 struct EpFfnLayout {
+  int P;  // grouped (received row, local expert) pair rows the buffers hold
   int groups, max_tiles, scale_ld;
   size_t err, counts, offsets, tile_group, tile_row0, tile_rows, num_tiles, pair_row, row_token, row_weight;
   size_t a_rows, a_scale, inter, inter_scale, total, head;
 };
 
-EpFfnLayout ep_ffn_layout(int R_max, int H, int I, int E_local, int top_k, int planes) {
+EpFfnLayout ep_ffn_layout(int R_max, int P_max, int H, int I, int E_local, int top_k, int planes) {
   EpFfnLayout L{};
-  const int P = std::max(R_max * top_k, 1);  // grouped pair rows
+  const int P = std::max(std::min(P_max, R_max * top_k), 1);  // grouped pair rows
+  L.P = P;
   L.groups = E_local;
   L.max_tiles = cdiv(P, kBlock) + E_local;
   L.scale_ld = static_cast<int>(align_up(P, 32));
@@ -329,9 +336,9 @@ int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* 
     return GEMMS_ERR_ARG;
   if (!aligned16(send_buf) || !aligned16(xq) || !aligned16(x_bf16)) return GEMMS_ERR_ALIGN;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
-  GEMMS_CUDA_TRY(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, st));
+  GEMMS_CUDA_TRY(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * 2 * world, st));
   if (T == 0) return GEMMS_OK;
-  ep_count_kernel<<<cdiv(T, 256), 256, 0, st>>>(topk_idx, T, top_k, E_local, send_counts);
+  ep_count_kernel<<<cdiv(T, 256), 256, 0, st>>>(topk_idx, T, top_k, E_local, world, send_counts);
   GEMMS_CUDA_TRY(cudaGetLastError());
   ep_assign_kernel<<<world, 1024, 0, st>>>(topk_idx, T, top_k, E_local, world, send_counts, send_row_of);
   GEMMS_CUDA_TRY(cudaGetLastError());
@@ -342,25 +349,25 @@ int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* 
   return GEMMS_OK;
 }
 
-size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t H, int32_t I, int32_t E_local, int32_t top_k,
-                                   int32_t inter_planes) {
+size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t P_max, int32_t H, int32_t I, int32_t E_local,
+                                   int32_t top_k, int32_t inter_planes) {
   const int planes = inter_planes == 0 ? 2 : inter_planes;
-  if (R_max < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
-      planes < 2 || planes > 3)
+  if (R_max < 0 || P_max < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 ||
+      top_k > 16 || planes < 2 || planes > 3)
     return 0;
-  return ep_ffn_layout(R_max, H, I, E_local, top_k, planes).total;
+  return ep_ffn_layout(R_max, P_max, H, I, E_local, top_k, planes).total;
 }
 
-int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, int32_t top_k, int32_t E_local,
-                        int32_t local_expert_offset, int32_t inter_planes, const void* w13, const float* w13_scale,
-                        const void* w2, const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
-                        gemms_stream_t stream_) {
+int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t H, int32_t I, int32_t top_k,
+                        int32_t E_local, int32_t local_expert_offset, int32_t inter_planes, const void* w13,
+                        const float* w13_scale, const void* w2, const float* w2_scale, float* out_rows,
+                        void* workspace, size_t ws_bytes, gemms_stream_t stream_) {
   const int planes = inter_planes == 0 ? 2 : inter_planes;
-  if (R < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
+  if (R < 0 || P_max < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
       planes < 2 || planes > 3)
     return GEMMS_ERR_SHAPE;
   if (!recv_buf || !w13 || !w13_scale || !w2 || !w2_scale || !out_rows) return GEMMS_ERR_ARG;
-  const EpFfnLayout L = ep_ffn_layout(R, H, I, E_local, top_k, planes);
+  const EpFfnLayout L = ep_ffn_layout(R, P_max, H, I, E_local, top_k, planes);
   if (!workspace || ws_bytes < L.total) return GEMMS_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GEMMS_ERR_ALIGN;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
@@ -386,6 +393,7 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
   pa.max_tiles = L.max_tiles;
+  pa.row_capacity = L.P;
   pa.err = err;
   if ((rc = launch_plan(pa, st))) return rc;
 
@@ -403,6 +411,7 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   sa.row_weight = at<float>(ws, L.row_weight);
   sa.pair_row = pair_row;
   sa.shared_rows = 0;
+  sa.row_capacity = L.P;
   if ((rc = launch_assign(sa, st))) return rc;
 
   PermuteArgs qa{};
@@ -429,7 +438,7 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, i
   gg.num_tiles = pa.num_tiles;
   gg.max_tiles = L.max_tiles;
   gg.shared_group = -1;
-  const int P = std::max(R * top_k, 1);
+  const int P = L.P;
 
   Gemm1Args g1{};
   g1.g = gg;

@@ -208,6 +208,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
   pa.max_tiles = L.max_tiles;
+  pa.row_capacity = L.R_max;
   pa.err = err;
   if ((rc = launch_plan(pa, st))) return rc;
 
@@ -223,6 +224,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   sa.row_weight = at<float>(ws, L.row_weight);
   sa.pair_row = ra.pair_row;
   sa.shared_rows = pa.shared_rows;
+  sa.row_capacity = L.R_max;
   if ((rc = launch_assign(sa, st))) return rc;
 
   PermuteArgs qa{};
@@ -433,6 +435,7 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
   pa.max_tiles = L.max_tiles;
+  pa.row_capacity = std::max(R_max, 1);
   pa.err = err;
   if ((rc = launch_plan(pa, st))) return rc;
 

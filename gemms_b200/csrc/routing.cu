@@ -215,6 +215,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
   if (tid == 0) {
     a.offsets[groups] = rows_total;
     a.num_tiles[0] = min(tiles_total, a.max_tiles);
+    if (rows_total > a.row_capacity) {  // counts disagree with the buffers' size: do no GEMM work
+      a.num_tiles[0] = 0;
+      atomicOr(a.err, kErrRowOverflow);
+    }
   }
 }
 
@@ -228,7 +232,7 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
   const int nwarps = blockDim.x >> 5;
   if (le == a.E_local) {  // shared expert group: row offsets[E_local] + t
     const int r0 = a.offsets[a.E_local];
-    for (int t = tid; t < a.T; t += blockDim.x) {
+    for (int t = tid; t < a.T && r0 + t < a.row_capacity; t += blockDim.x) {
       a.row_token[r0 + t] = t;
       a.row_weight[r0 + t] = 1.0f;
     }
@@ -259,8 +263,8 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
     __syncthreads();
     const int warp_excl = (warp > 0 ? s_warp[warp - 1] : 0);
     const int base = s_base;
-    if (jsel >= 0) {
-      const int r = base + warp_excl + __popc(ballot & ((1u << lane) - 1u));
+    const int r = base + warp_excl + __popc(ballot & ((1u << lane) - 1u));
+    if (jsel >= 0 && r < a.row_capacity) {
       a.row_token[r] = t;
       a.row_weight[r] = a.topk_w[(size_t)t * stride + jsel];
       a.pair_row[(size_t)t * a.top_k + jsel] = r;

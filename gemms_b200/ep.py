@@ -106,7 +106,7 @@ class CudaEpKernels:
         k = idx.shape[1]
         dev = x.device
         rb = row_bytes(H, k)
-        send_counts = torch.empty((world,), dtype=torch.int32, device=dev)
+        send_counts = torch.empty((2, world), dtype=torch.int32, device=dev)  # rows, pairs per destination
         send_row_of = torch.empty((T, world), dtype=torch.int32, device=dev)
         send_buf = torch.empty((max(T * min(world, k), 1), rb), dtype=torch.uint8, device=dev)
         xq = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
@@ -117,15 +117,16 @@ class CudaEpKernels:
                    "gemms_ep_dispatch")
         return send_counts, send_row_of, send_buf, xq, xq_scale
 
-    def expert_ffn(self, recv_buf, R: int, H: int, I: int, top_k: int, E_local: int, offset: int, planes: int,
-                   w13, w13_scale, w2, w2_scale):
+    def expert_ffn(self, recv_buf, R: int, P: int, H: int, I: int, top_k: int, E_local: int, offset: int,
+                   planes: int, w13, w13_scale, w2, w2_scale):
+        """Received rows -> fp32 [R, H]; P = (row, local expert) pairs they name."""
         dev = w13.device
         out = torch.empty((max(R, 1), H), dtype=torch.float32, device=dev)
-        nbytes = self.L.gemms_ep_ffn_workspace_size(R, H, I, E_local, top_k, planes)
+        nbytes = self.L.gemms_ep_ffn_workspace_size(R, P, H, I, E_local, top_k, planes)
         if nbytes == 0:
             raise ValueError("unsupported expert-parallel FFN geometry")
         ws = self._workspace(dev, nbytes, "ep_ffn")
-        _lib.check(self.L.gemms_ep_expert_ffn(recv_buf.data_ptr(), R, H, I, top_k, E_local, offset, planes,
+        _lib.check(self.L.gemms_ep_expert_ffn(recv_buf.data_ptr(), R, P, H, I, top_k, E_local, offset, planes,
                                               w13.data_ptr(), w13_scale.data_ptr(), w2.data_ptr(),
                                               w2_scale.data_ptr(), out.data_ptr(), ws.data_ptr(), nbytes,
                                               self._stream()), "gemms_ep_expert_ffn")
@@ -279,14 +280,17 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     send_counts, send_row_of, send_buf, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local)
     mark("pack")
 
-    # count matrix m[src, dst] on every rank: this rank's send and receive
-    # counts, and (peer combine) where its rows sit in each destination's order
+    # count matrices on every rank: m[src][dst] rows and mp[src][dst] routed
+    # pairs -- this rank's send and receive counts, the size of its grouped
+    # rows, and (peer combine) where its rows sit in each destination's order
     gathered = [torch.empty_like(send_counts) for _ in range(world)]
     dist.all_gather(gathered, send_counts, group=group)
-    m = torch.stack(gathered).cpu().tolist()  # the one host synchronisation of the layer
+    both = torch.stack(gathered).cpu().tolist()  # the one host synchronisation of the layer
+    m = [b[0] for b in both]
     sc = [int(v) for v in m[rank]]
     rc = [int(m[src][rank]) for src in range(world)]
     S, R = sum(sc), sum(rc)
+    P = sum(int(b[1][rank]) for b in both)
     mark("count_exchange")
     if timeline is not None:
         timeline.append(("recv_rows", R))
@@ -319,7 +323,7 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
         per_expert.scatter_add_(0, slot, torch.ones_like(slot))
         stats = (valid.sum(), per_expert[:E_local])
 
-    out_rows = K.expert_ffn(recv_buf, R, H, I, top_k, E_local, rank * E_local, inter_planes,
+    out_rows = K.expert_ffn(recv_buf, R, P, H, I, top_k, E_local, rank * E_local, inter_planes,
                             w13, w13_scale, w2, w2_scale)
     mark("expert_ffn")
     if combine == "peer":

@@ -176,7 +176,9 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
 size_t gemms_ep_row_bytes(int32_t H, int32_t top_k);
 
 /* topk_idx/topk_w [T, top_k] (global ids) + x bf16 [T, H] ->
- * send_counts [world] (zeroed here), send_row_of [T, world] (-1 = not sent),
+ * send_counts int32 [2, world] (zeroed here): [0][d] rows sent to rank d and
+ * [1][d] routed (token, expert) pairs they carry for d's experts (the sizes
+ * of d's grouped rows), send_row_of [T, world] (-1 = not sent),
  * send_buf [<= T*min(world,top_k), row_bytes] grouped by destination in token
  * order, and the token-major quantised rows xq [T, H] + xq_scale [H/128, T]. */
 int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* x_bf16, int32_t T, int32_t H,
@@ -184,13 +186,17 @@ int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* 
                       void* send_buf, void* xq, float* xq_scale, gemms_stream_t stream);
 
 /* Received packed rows [R, row_bytes] -> out_rows fp32 [R, H] (overwritten):
- * each row's results summed over its experts on this rank, times weights. */
-size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t H, int32_t I, int32_t E_local, int32_t top_k,
-                                   int32_t inter_planes);
-int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t H, int32_t I, int32_t top_k, int32_t E_local,
-                        int32_t local_expert_offset, int32_t inter_planes, const void* w13, const float* w13_scale,
-                        const void* w2, const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
-                        gemms_stream_t stream);
+ * each row's results summed over its experts on this rank, times weights.
+ * P_max bounds the (row, local expert) pairs the rows name (the sum over
+ * sources of their send_counts[1][this rank]); the workspace holds that many
+ * grouped rows.  Rows beyond it are not computed and set GEMMS_FLAG_ROW_OVERFLOW
+ * in the workspace's error word (gemms_moe_check). */
+size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t P_max, int32_t H, int32_t I, int32_t E_local,
+                                   int32_t top_k, int32_t inter_planes);
+int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t H, int32_t I, int32_t top_k,
+                        int32_t E_local, int32_t local_expert_offset, int32_t inter_planes, const void* w13,
+                        const float* w13_scale, const void* w2, const float* w2_scale, float* out_rows,
+                        void* workspace, size_t ws_bytes, gemms_stream_t stream);
 
 /* Packed combine row: fp16 [H] holding value / 2^e | fp32 2^e | pad to 16 B,
  * with 2^e the power of two that puts max|row| / 2^e in [2^14, 2^15) (e = 0

@@ -42,13 +42,14 @@ class CpuEpKernels:
         dests = (idx.long() // E_local)
         send_row_of = torch.full((T, world), -1, dtype=torch.int32)
         rows = []
-        counts = torch.zeros(world, dtype=torch.int32)
+        counts = torch.zeros((2, world), dtype=torch.int32)  # rows, routed pairs per destination
         for d in range(world):
             for t in range(T):
                 if bool((dests[t] == d).any()):
                     send_row_of[t, d] = len(rows)
                     rows.append((t, d))
-                    counts[d] += 1
+                    counts[0, d] += 1
+                    counts[1, d] += int((dests[t] == d).sum())
         buf = torch.zeros((max(len(rows), 1), rb), dtype=torch.uint8)
         for r, (t, d) in enumerate(rows):
             buf[r, :H] = xq[t].view(torch.uint8)
@@ -60,7 +61,7 @@ class CpuEpKernels:
             buf[r, H + 4 * KB + 4 * k:H + 4 * KB + 8 * k] = ws.view(torch.uint8)
         return counts, send_row_of, buf, xq, xq_scale
 
-    def expert_ffn(self, recv_buf, Rn, H, I, top_k, E_local, offset, planes, w13, w13_scale, w2, w2_scale):
+    def expert_ffn(self, recv_buf, Rn, P, H, I, top_k, E_local, offset, planes, w13, w13_scale, w2, w2_scale):
         KB = H // BLOCK
         out = torch.zeros((Rn, H), dtype=torch.float32)
         if Rn == 0:
