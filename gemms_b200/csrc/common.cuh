@@ -146,6 +146,7 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
 
 // Router GEMM (router_gemm.cu): logits = x . router_w^T via a bf16 hi/lo split.
 struct RouterPlan {
+  int simt;          // 1: CUDA-core fp32 path (decode-sized T), no weight planes
   int Np;            // E rounded up to 16 (MMA N)
   int KB;            // 64-element K blocks
   int kb_per_split;

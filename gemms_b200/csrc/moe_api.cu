@@ -61,7 +61,7 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.out_acc = take(sizeof(float) * (size_t)L.T * L.H);
   if (s.input_mode == GEMMS_INPUT_BF16) {
     L.router = router_plan(s.T, s.H, s.E);
-    L.router_planes = take(L.router.split_bytes);
+    L.router_planes = L.router.split_bytes ? take(L.router.split_bytes) : 0;
     L.router_partials = take(L.router.partial_bytes);
   }
   L.total = o;
@@ -169,7 +169,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
     rg.T = s.T;
     rg.H = s.H;
     rg.E = s.E;
-    rg.planes = at<__nv_bfloat16>(ws, L.router_planes);
+    rg.planes = L.router.split_bytes ? at<__nv_bfloat16>(ws, L.router_planes) : nullptr;
     rg.partials = at<float>(ws, L.router_partials);
     rg.err = err;
     if ((rc = launch_router_gemm(rg, st))) return rc;

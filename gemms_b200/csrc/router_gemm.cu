@@ -12,6 +12,10 @@
 // fp32 partial [128 x E] to partials[split][t][e] and route_kernel sums the
 // splits in a fixed order (deterministic, no atomics).
 //
+// Decode-sized batches (T <= 128) take a CUDA-core path instead: fp32 FMAs
+// over x (bf16, exact in fp32) and router_w read once in fp32, so no bf16
+// weight planes are needed; the same split-K partials and fixed-order sum.
+//
 // CTA: 128 threads.  Thread 0 issues TMA loads of the x tile [128 x 64 bf16]
 // and both weight planes [N x 64 bf16] (128-byte swizzle) into a 2-stage ring;
 // warp 1 allocates TMEM and one of its threads issues tcgen05.mma.kind::f16
@@ -34,6 +38,8 @@ constexpr int RBK = 64;                 // bf16 elements per K block = 128 bytes
 constexpr int kStages = 2;
 constexpr int kThreads = 128;
 constexpr int kSplitTarget = 148;       // B200 SM count: aim at one CTA per SM
+constexpr int kSimtMaxT = 128;          // decode-sized batches: CUDA-core fp32 path
+constexpr int kSimtExperts = 16;        // experts per CTA (two per warp)
 
 __host__ __device__ inline int pad16(int e) { return (e + 15) / 16 * 16; }
 
@@ -77,6 +83,70 @@ __global__ void router_split_kernel(const float* __restrict__ w, __nv_bfloat16* 
     *reinterpret_cast<uint2*>(planes + per_plane + o) = lv;
   }
 }
+
+// (a0, a1) += (x0, x1) * (w0, w1), one packed fp32x2 FMA.
+__device__ __forceinline__ void ffma2v(float& a0, float& a1, float x0, float x1, float w0, float w1) {
+  asm("{\n\t.reg .b64 acc, xv, wv;\n\t"
+      "mov.b64 acc, {%0, %1};\n\t"
+      "mov.b64 xv, {%2, %3};\n\t"
+      "mov.b64 wv, {%4, %5};\n\t"
+      "fma.rn.f32x2 acc, xv, wv, acc;\n\t"
+      "mov.b64 {%0, %1}, acc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(w0), "f"(w1));
+}
+
+// Decode path: CTA = 8 warps = 16 experts (two per warp), split = K chunk of
+// KC elements; every lane owns KC/32 consecutive columns of both experts' fp32
+// rows in registers and streams the T tokens' bf16 columns past them.  Sums
+// per lane in a fixed order, then a butterfly over the warp: deterministic.
+template <int KC>
+__global__ void __launch_bounds__(256) router_simt_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const float* __restrict__ w, int T, int H, int E,
+                                                          float* __restrict__ partials) {
+  constexpr int PER = KC / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * kSimtExperts + 2 * warp;
+  const int split = blockIdx.y;
+  const int k0 = split * KC + lane * PER;
+  float wa[PER], wb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; j += 4) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (e0 < E) a = __ldg(reinterpret_cast<const float4*>(w + (size_t)e0 * H + k0 + j));
+    if (e0 + 1 < E) b = __ldg(reinterpret_cast<const float4*>(w + (size_t)(e0 + 1) * H + k0 + j));
+    wa[j] = a.x; wa[j + 1] = a.y; wa[j + 2] = a.z; wa[j + 3] = a.w;
+    wb[j] = b.x; wb[j + 1] = b.y; wb[j + 2] = b.z; wb[j + 3] = b.w;
+  }
+  for (int t = 0; t < T; ++t) {
+    const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)t * H + k0);
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j += 8) {
+      const uint4 raw = __ldg(xp + j / 8);
+      const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 xv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[q]));
+        ffma2v(a0, a1, xv.x, xv.y, wa[j + 2 * q], wa[j + 2 * q + 1]);
+        ffma2v(b0, b1, xv.x, xv.y, wb[j + 2 * q], wb[j + 2 * q + 1]);
+      }
+    }
+    float sa = a0 + a1, sb = b0 + b1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, off);
+      sb += __shfl_xor_sync(0xffffffffu, sb, off);
+    }
+    if (lane == 0) {
+      float* dst = partials + ((size_t)split * T + t) * E;
+      if (e0 < E) dst[e0] = sa;
+      if (e0 + 1 < E) dst[e0 + 1] = sb;
+    }
+  }
+}
+
+int simt_chunk(int H) { return H % 1024 == 0 ? 1024 : (H % 512 == 0 ? 512 : 256); }
 
 struct RouterParams {
   int T, E, Np, KB, kb_per_split;
@@ -236,6 +306,15 @@ uint32_t tmem_cols_for(int n) {
 
 RouterPlan router_plan(int T, int H, int E) {
   RouterPlan r{};
+  if (T <= kSimtMaxT && H % 256 == 0) {  // CUDA-core path: no weight planes
+    r.simt = 1;
+    r.KB = H / simt_chunk(H);
+    r.kb_per_split = 1;
+    r.splits = r.KB;
+    r.split_bytes = 0;
+    r.partial_bytes = align_up(sizeof(float) * (size_t)r.splits * std::max(T, 1) * E, 256);
+    return r;
+  }
   r.Np = pad16(E);
   r.KB = H / RBK;
   const int m_tiles = std::max(1, cdiv(T, RBM));
@@ -250,9 +329,22 @@ RouterPlan router_plan(int T, int H, int E) {
 int launch_router_gemm(const RouterGemmArgs& a, cudaStream_t s) {
   if (a.T <= 0) return GEMMS_OK;
   if (a.H % RBK || a.E < 1 || a.E > 256) return GEMMS_ERR_SHAPE;
+  const RouterPlan& r = a.plan;
+  if (r.simt) {
+    if (!aligned16(a.x) || !aligned16(a.router_w) || (a.H % 8)) return GEMMS_ERR_ALIGN;
+    const dim3 grid(cdiv(a.E, kSimtExperts), r.splits);
+    const int kc = simt_chunk(a.H);
+    if (kc == 1024)
+      router_simt_kernel<1024><<<grid, 256, 0, s>>>(a.x, a.router_w, a.T, a.H, a.E, a.partials);
+    else if (kc == 512)
+      router_simt_kernel<512><<<grid, 256, 0, s>>>(a.x, a.router_w, a.T, a.H, a.E, a.partials);
+    else
+      router_simt_kernel<256><<<grid, 256, 0, s>>>(a.x, a.router_w, a.T, a.H, a.E, a.partials);
+    GEMMS_CUDA_TRY(cudaGetLastError());
+    return GEMMS_OK;
+  }
   if (!aligned16(a.x) || !aligned16(a.router_w) || !aligned16(a.planes) || !aligned16(a.partials))
     return GEMMS_ERR_ALIGN;
-  const RouterPlan& r = a.plan;
   const int nsplit = static_cast<int>(std::min<size_t>(((size_t)r.Np * a.H / 4 + 255) / 256, (size_t)num_sms() * 4));
   router_split_kernel<<<nsplit, 256, 0, s>>>(a.router_w, a.planes, a.E, r.Np, a.H);
   GEMMS_CUDA_TRY(cudaGetLastError());
@@ -315,7 +407,7 @@ extern "C" int gemms_router_logits(const void* x_bf16, const float* router_w, in
   a.H = H;
   a.E = E;
   a.err = reinterpret_cast<int*>(ws);
-  a.planes = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+  a.planes = a.plan.split_bytes ? reinterpret_cast<__nv_bfloat16*>(ws + 256) : nullptr;
   a.partials = reinterpret_cast<float*>(ws + 256 + a.plan.split_bytes);
   GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, st));
   int rc = launch_router_gemm(a, st);

@@ -116,18 +116,20 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
  * No counterpart in the reference.  Scratch is a fixed 16 MiB device array
  * inside this library, held by every GPU that loads it until process exit;
  * shapes whose gemms_moe_workspace_size() exceeds 16 MiB are rejected with
- * GEMMS_ERR_CAPACITY (DeepSeek-V3 shapes with a shared expert: up to 126
- * tokens).  The first call on a device looks up the array's device address
+ * GEMMS_ERR_CAPACITY (DeepSeek-V3 shapes with a shared expert: up to 119
+ * tokens when the layer computes the router logits from bf16 activations,
+ * 126 with given logits and FP8 activations).  The first call on a device looks up the array's device address
  * (make it before any stream capture).  All calls share the array: calls that
  * overlap on the GPU (other streams, other host threads) race.  Allocates
  * nothing. */
 int gemms_moe_fwd_noalloc(const GemmsMoeArgs* args, gemms_stream_t stream);
 
 /* Router GEMM alone: logits fp32 [T, E] = x bf16 [T, H] . router_w fp32
- * [E, H]^T (H a multiple of 64, E <= 256), computed as x . hi^T + x . lo^T
+ * [E, H]^T (H a multiple of 64, E <= 256).  T > 128: x . hi^T + x . lo^T
  * with router_w = hi + lo + r split into two bf16 planes (|r| <= 2^-16 |w|)
- * and fp32 accumulation on the tensor cores; deterministic (split-K partials
- * are summed in a fixed order).  Workspace: gemms_router_workspace_size().
+ * and fp32 accumulation on the tensor cores; T <= 128 (decode): fp32 FMAs on
+ * the CUDA cores over router_w as given.  Deterministic (split-K partials are
+ * summed in a fixed order).  Workspace: gemms_router_workspace_size().
  * No counterpart in the reference, which takes logits as input
  * (flashinfer_baseline.py:6). */
 size_t gemms_router_workspace_size(int32_t T, int32_t H, int32_t E);
