@@ -44,6 +44,7 @@ EXPORTS = (
     "gemms_router_workspace_size",
     "gemms_router_logits",
     "gemms_quantize_1x128",
+    "gemms_rmsnorm_quant",
 )
 
 
@@ -65,7 +66,7 @@ class GemmsMoeArgs(ctypes.Structure):
         ("shared_w13", c_void_p), ("shared_w13_scale", c_void_p), ("shared_w2", c_void_p),
         ("shared_w2_scale", c_void_p),
         ("out", c_void_p), ("topk_idx_out", c_void_p), ("topk_w_out", c_void_p), ("expert_counts_out", c_void_p),
-        ("profile_events", c_void_p), ("router_w", c_void_p), ("logits_out", c_void_p),
+        ("profile_events", c_void_p), ("router_w", c_void_p), ("logits_out", c_void_p), ("residual", c_void_p),
     ]
 
 
@@ -167,6 +168,9 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_router_logits.restype = c_int32
         L.gemms_quantize_1x128.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]
         L.gemms_quantize_1x128.restype = c_int32
+        L.gemms_rmsnorm_quant.argtypes = [c_void_p, c_void_p, c_int32, c_float, c_int32, c_int32, c_void_p, c_void_p,
+                                          c_void_p, c_void_p]
+        L.gemms_rmsnorm_quant.restype = c_int32
         _lib = L
         return L
 

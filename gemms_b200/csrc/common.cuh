@@ -107,8 +107,8 @@ int launch_permute(const PermuteArgs& a, cudaStream_t s);
 // Token-major per-1x128 quantisation: bf16 [T, H] -> e4m3 [T, H] + fp32 scale [H/128, T].
 int launch_quantize(const __nv_bfloat16* x, int T, int H, uint8_t* xq, float* xq_scale, cudaStream_t s);
 
-// fp32 [n] -> bf16 [n]
-int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s);
+// fp32 [n] (+ optional bf16 residual [n]) -> bf16 [n], one rounding
+int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, const __nv_bfloat16* residual, cudaStream_t s);
 
 // Grouped block-scaled FP8 GEMMs.
 struct GemmGroupsArgs {

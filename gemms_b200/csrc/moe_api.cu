@@ -296,7 +296,9 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   if ((rc = launch_gemm2(g2, st))) return rc;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[2], st));
 
-  if ((rc = launch_to_bf16(g2.out, static_cast<__nv_bfloat16*>(args->out), (size_t)s.T * s.H, st))) return rc;
+  if ((rc = launch_to_bf16(g2.out, static_cast<__nv_bfloat16*>(args->out), (size_t)s.T * s.H,
+                           static_cast<const __nv_bfloat16*>(args->residual), st)))
+    return rc;
 
   if (args->topk_idx_out)
     GEMMS_CUDA_TRY(cudaMemcpyAsync(args->topk_idx_out, ra.topk_idx, sizeof(int32_t) * (size_t)s.T * s.top_k,

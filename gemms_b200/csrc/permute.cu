@@ -113,9 +113,19 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __re
   }
 }
 
-__global__ void to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, size_t n4) {
+__global__ void to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, size_t n4,
+                               const uint2* __restrict__ residual) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = in[i];
+    float4 v = in[i];
+    if (residual) {  // the decoder's residual add, fused: one rounding of (residual + layer)
+      const uint2 r = residual[i];
+      const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+      const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+      v.x += r0.x;
+      v.y += r0.y;
+      v.z += r1.x;
+      v.w += r1.y;
+    }
     __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
     __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
     uint2 o;
@@ -146,12 +156,14 @@ int launch_quantize(const __nv_bfloat16* x, int T, int H, uint8_t* xq, float* xq
   return GEMMS_OK;
 }
 
-int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, cudaStream_t s) {
+int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, const __nv_bfloat16* residual, cudaStream_t s) {
   if (n == 0) return GEMMS_OK;
   if (n % 4) return GEMMS_ERR_SHAPE;
+  if (residual && (reinterpret_cast<uintptr_t>(residual) & 7u)) return GEMMS_ERR_ALIGN;
   const size_t n4 = n / 4;
   const int blocks = static_cast<int>(std::min<size_t>((n4 + 255) / 256, (size_t)num_sms() * 8));
-  to_bf16_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(in), reinterpret_cast<uint2*>(out), n4);
+  to_bf16_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(in), reinterpret_cast<uint2*>(out), n4,
+                                        reinterpret_cast<const uint2*>(residual));
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

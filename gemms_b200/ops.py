@@ -211,7 +211,7 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         shared_w2: torch.Tensor | None = None, shared_w2_scale: torch.Tensor | None = None,
         n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
         inter_planes: int = 2, logits: torch.Tensor | None = None, ep_group=None,
-        return_routing: bool = False, profile_events=None):
+        return_routing: bool = False, profile_events=None, residual: torch.Tensor | None = None):
     """DeepSeek-V3 MoE layer forward: bf16 x [T, H] -> bf16 [T, H].
 
     ``w13`` [E, 2I, H] / ``w2`` [E, H, I] are e4m3 with fp32 128x128 block
@@ -220,8 +220,12 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
     E/world experts and tokens are exchanged with NCCL all-to-all.
     ``logits`` overrides the router GEMM.  ``profile_events`` (three recorded
     ``torch.cuda.Event``) brackets GEMM1 and GEMM2 for kernel timing.
+    ``residual`` (bf16 [T, H]) is added to the layer's fp32 result before the
+    single rounding to bf16 (the decoder's residual add, fused).
     """
     if ep_group is not None:
+        if residual is not None:
+            raise ShapeError("residual is not supported with ep_group")
         from . import ep
         return ep.moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13=shared_w13,
                          shared_w13_scale=shared_w13_scale, shared_w2=shared_w2, shared_w2_scale=shared_w2_scale,
@@ -230,7 +234,7 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
                          logits=logits, group=ep_group)
     has_shared = shared_w13 is not None
     dev = _check_cuda(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13, shared_w13_scale,
-                      shared_w2, shared_w2_scale, logits)
+                      shared_w2, shared_w2_scale, logits, residual)
     _req(x.dim() == 2 and x.dtype == torch.bfloat16, "x must be bf16 [T, H]")
     T, H = x.shape
     _req(w13.dim() == 3 and w13.shape[2] == H, "w13 must be [E, 2I, H]")
@@ -265,6 +269,9 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         args.shared_w13, args.shared_w13_scale = _ptr(shared_w13), _ptr(shared_w13_scale)
         args.shared_w2, args.shared_w2_scale = _ptr(shared_w2), _ptr(shared_w2_scale)
     args.out = _ptr(out)
+    if residual is not None:
+        _req(residual.shape == (T, H) and residual.dtype == torch.bfloat16, "residual must be bf16 [T, H]")
+        args.residual = _ptr(residual)
     idx = w = counts = None
     if return_routing:
         idx = torch.empty((T, top_k), dtype=torch.int32, device=dev)
@@ -302,6 +309,71 @@ def quantize_1x128(x: torch.Tensor):
     _lib.check(L.gemms_quantize_1x128(x.data_ptr(), T, H, xq.data_ptr(), sc.data_ptr(), _stream()),
                "gemms_quantize_1x128")
     return xq, sc
+
+
+@torch.no_grad()
+@_on_tensor_device
+def rmsnorm_quant(h: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6):
+    """DeepSeek-V3 RMSNorm fused with the per-1x128 quantisation
+    (``gemms_rmsnorm_quant``): h bf16 [T, H] -> (y bf16 [T, H], xq e4m3
+    [T, H], scale fp32 [H/128, T]), y = weight * bf16(h * rsqrt(mean(h^2) +
+    eps)) rounded to bf16 and (xq, scale) its 1x128 quantisation."""
+    dev = _check_cuda(h, weight)
+    _req(h.dim() == 2 and h.dtype == torch.bfloat16, "h must be bf16 [T, H]")
+    T, H = h.shape
+    _req(H % BLOCK == 0, "H must be a multiple of 128")
+    _req(weight.shape == (H,) and weight.dtype in (torch.bfloat16, torch.float32), "weight must be bf16/fp32 [H]")
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    xq = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+    sc = torch.empty((H // BLOCK, T), dtype=torch.float32, device=dev)
+    L = _lib.load()
+    _lib.check(L.gemms_rmsnorm_quant(h.data_ptr(), weight.data_ptr(), int(weight.dtype == torch.bfloat16), float(eps),
+                                     T, H, y.data_ptr(), xq.data_ptr(), sc.data_ptr(), _stream()),
+               "gemms_rmsnorm_quant")
+    return y, xq, sc
+
+
+@torch.no_grad()
+@_on_tensor_device
+def moe_block(h: torch.Tensor, norm_weight: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor,
+              w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor, *,
+              eps: float = 1e-6, shared_w13: torch.Tensor | None = None, shared_w13_scale: torch.Tensor | None = None,
+              shared_w2: torch.Tensor | None = None, shared_w2_scale: torch.Tensor | None = None,
+              n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
+              inter_planes: int = 2) -> torch.Tensor:
+    """The MoE half of a DeepSeek-V3 decoder layer on the residual stream h
+    (bf16 [T, H]): h + moe(rmsnorm(h)).  RMSNorm and the 1x128 quantisation
+    run as one kernel whose e4m3 rows feed the experts directly (no second
+    quantisation); the router GEMM reads the bf16 normalised rows; the
+    residual add is fused into the layer's final cast (one rounding)."""
+    dev = _check_cuda(h, norm_weight, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13,
+                      shared_w13_scale, shared_w2, shared_w2_scale)
+    y, xq, xq_scale = rmsnorm_quant(h, norm_weight, eps)
+    logits = router_logits(y, router_w)
+    T, H = h.shape
+    E, twoI, _ = w13.shape
+    I = twoI // 2
+    _req(router_w.shape == (E, H) and router_bias.shape[-1] == E, "router_w / router_bias shapes")
+    _req(w13.dtype == torch.float8_e4m3fn and w2.dtype == torch.float8_e4m3fn, "weights must be e4m3")
+    _req(w2.shape == (E, H, I), "w2 must be [E, H, I]")
+    has_shared = shared_w13 is not None
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    shape = GemmsMoeShape(T=T, H=H, I=I, E=E, E_local=E, local_expert_offset=0, n_group=n_group,
+                          topk_group=topk_group, top_k=top_k, has_shared=int(has_shared),
+                          input_mode=_lib.GEMMS_INPUT_FP8, bias_bf16=int(router_bias.dtype == torch.bfloat16),
+                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor))
+    args = GemmsMoeArgs()
+    args.routing_logits = _ptr(logits)
+    args.routing_bias = _ptr(router_bias)
+    args.hidden_fp8, args.hidden_scale = _ptr(xq), _ptr(xq_scale)
+    args.w13, args.w13_scale, args.w2, args.w2_scale = _ptr(w13), _ptr(w13_scale), _ptr(w2), _ptr(w2_scale)
+    if has_shared:
+        args.shared_w13, args.shared_w13_scale = _ptr(shared_w13), _ptr(shared_w13_scale)
+        args.shared_w2, args.shared_w2_scale = _ptr(shared_w2), _ptr(shared_w2_scale)
+    args.out = _ptr(out)
+    args.residual = _ptr(h)
+    _call_fwd(shape, args, dev, "moe_block")
+    return out
 
 
 @torch.no_grad()

@@ -99,6 +99,9 @@ typedef struct {
                                     /* GEMMS_INPUT_BF16, logits = x . router_w^T   */
                                     /* on the tensor cores (bf16 hi/lo split)      */
   float* logits_out;                /* optional fp32 [T, E]: the logits used       */
+  const void* residual;             /* optional bf16 [T, H]: out = bf16(residual + */
+                                    /* layer), one rounding (the decoder's         */
+                                    /* residual add after the MoE block)           */
 } GemmsMoeArgs;
 
 /* Bytes of device workspace gemms_moe_fwd needs for this shape. */
@@ -144,6 +147,17 @@ int gemms_router_logits(const void* x_bf16, const float* router_w, int32_t T, in
  * activations). */
 int gemms_quantize_1x128(const void* x_bf16, int32_t T, int32_t H, void* xq, float* xq_scale,
                          gemms_stream_t stream);
+
+/* The step before the layer: RMSNorm fused with the per-1x128 quantisation.
+ * h bf16 [T, H] (H a multiple of 128), weight bf16 (weight_bf16 = 1) or fp32
+ * [H] ->  y = weight * bf16(h * rsqrt(mean(h^2) + eps)) rounded to bf16 (the
+ * DeepSeek-V3 RMSNorm) into y_bf16 [T, H] (optional: the router GEMM's
+ * input), and its 1x128 e4m3 quantisation into xq [T, H] + xq_scale
+ * [H/128, T] (optional, as gemms_quantize_1x128: the experts' input with
+ * GEMMS_INPUT_FP8).  No counterpart in the reference (its operator starts
+ * from quantised activations, flashinfer_baseline.py:5-16). */
+int gemms_rmsnorm_quant(const void* h_bf16, const void* weight, int32_t weight_bf16, float eps, int32_t T,
+                        int32_t H, void* y_bf16, void* xq, float* xq_scale, gemms_stream_t stream);
 
 /* Router only (for tests and expert-parallel dispatch): fp32 logits [T,E] +
  * bias -> topk_idx int32 [T,top_k] (descending biased score), topk_w fp32

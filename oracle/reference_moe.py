@@ -249,6 +249,33 @@ def moe_layer(x, router_w, router_bias, w13, w13_scale, w2, w2_scale,
     return out if return_fp32 else out.to(torch.bfloat16)
 
 
+# --------------------------------------------------------------------------
+# The steps either side of the layer (no reference code: the reference's
+# operator starts from quantised activations).  RMSNorm as the DeepSeek-V3
+# decoder defines it: fp32 variance and rsqrt, cast back to the activations'
+# dtype, times the weight.  Parity unpinned.
+# --------------------------------------------------------------------------
+def rmsnorm(h: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """y = weight * bf16(h * rsqrt(mean(h^2) + eps)), rounded to bf16."""
+    hs = h.to(torch.float32)
+    var = hs.pow(2).mean(-1, keepdim=True)
+    hs = hs * torch.rsqrt(var + eps)
+    return (weight.to(torch.float32) * hs.to(h.dtype).to(torch.float32)).to(torch.bfloat16)
+
+
+@torch.no_grad()
+def moe_block(h, norm_weight, router_w, router_bias, w13, w13_scale, w2, w2_scale,
+              shared_w13=None, shared_w13_scale=None, shared_w2=None, shared_w2_scale=None, *,
+              n_group, topk_group, top_k, rsf, eps=1e-6, logits=None, tokens=None):
+    """h + moe(rmsnorm(h)) with the residual added to the layer's fp32 result
+    and rounded to bf16 once."""
+    y = rmsnorm(h, norm_weight, eps)
+    out = moe_layer(y, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13, shared_w13_scale,
+                    shared_w2, shared_w2_scale, n_group=n_group, topk_group=topk_group, top_k=top_k, rsf=rsf,
+                    logits=logits, tokens=tokens, return_fp32=True)
+    return (out + h.to(torch.float32)).to(torch.bfloat16)
+
+
 def compare(out: torch.Tensor, ref: torch.Tensor, rows=None) -> dict:
     """Output parity metrics used by every layer test.
 
