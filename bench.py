@@ -400,10 +400,26 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 8, 32, 128), steps=50, warmup=5):
         e1.record()
         e1.synchronize()
         ms = e0.elapsed_time(e1) / steps
+        # the same layer captured in a CUDA graph (gemms_b200.MoeGraph): one
+        # launch per step instead of one per kernel
+        graph = gemms_b200.MoeGraph(d, T, **kw)
+        for _ in range(warmup):
+            graph(x)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            graph(x)
+        e1.record()
+        e1.synchronize()
+        ms_g = e0.elapsed_time(e1) / steps
+        del graph
         nbytes = (hit + (1 if sh.shared else 0)) * sh.expert_bytes()
         gbs = nbytes / (ms / 1e3) / 1e9
+        gbs_g = nbytes / (ms_g / 1e3) / 1e9
         res[f"T={T}"] = {"ms_per_step": round(ms, 5), "tokens_per_s": round(T / (ms / 1e3), 1), "experts_hit": hit,
-                         "weight_bytes": nbytes, "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)}
+                         "weight_bytes": nbytes, "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                         "graph": {"ms_per_step": round(ms_g, 5), "tokens_per_s": round(T / (ms_g / 1e3), 1),
+                                   "GB/s": round(gbs_g, 1), "hbm_frac": round(gbs_g / hbm, 4)}}
     return res
 
 
@@ -573,7 +589,8 @@ def gpu_arm(a):
         line["decode_c2"] = {"what": "BASELINE config c2 on the same GPU and weights: full layer (router GEMM, "
                                      "routing, quantisation, grouped GEMMs, combine, shared expert) on the first T "
                                      "tokens; GB/s = weight bytes of the experts hit (+ shared) per layer / time; "
-                                     "hbm_frac against the measured HBM copy bandwidth",
+                                     "hbm_frac against the measured HBM copy bandwidth; 'graph': the same call "
+                                     "replayed from a CUDA graph (gemms_b200.MoeGraph)",
                              **decode}
     if group is not None:
         # Dominant phase at N>1: the grouped GEMMs over the received rows

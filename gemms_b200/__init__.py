@@ -13,6 +13,7 @@ Public operators (CUDA tensors only, no CPU fallback):
   layer: RMSNorm fused with the quantisation, and h + moe(rmsnorm(h)) with
   the residual add fused into the layer's output cast.
 * :class:`MoePipeline` -- host-to-host serving loop with PCIe copies overlapped.
+* :class:`MoeGraph` -- one decode-sized layer call captured in a CUDA graph.
 * ``torch.ops.gemms_b200.moe`` / ``torch.ops.gemms_b200.run`` -- the same layer
   as PyTorch dispatcher operators (after :func:`load_torch_ops`).
 """
@@ -20,8 +21,8 @@ from .ops import (ShapeError, check_device_errors, moe, moe_block, quantize_1x12
                   router_logits, run)
 from ._lib import GemmsError, lib_path, load as load_library, load_torch_ops  # noqa: F401
 from . import workloads  # noqa: F401
-from .pipeline import MoePipeline  # noqa: F401
+from .pipeline import MoeGraph, MoePipeline  # noqa: F401
 
 __all__ = ["run", "moe", "moe_block", "route", "router_logits", "quantize_1x128", "rmsnorm_quant", "ShapeError", "GemmsError", "check_device_errors",
-           "load_library", "load_torch_ops", "lib_path", "workloads", "MoePipeline"]
+           "load_library", "load_torch_ops", "lib_path", "workloads", "MoePipeline", "MoeGraph"]
 __version__ = "0.1.0"

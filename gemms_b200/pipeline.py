@@ -78,3 +78,46 @@ class MoePipeline:
                 self.ev_out[k].record(self.s_out)
             self.used[k] = True
         self.s_out.synchronize()
+
+
+class MoeGraph:
+    """One ``ops.moe`` call for a fixed token count captured in a CUDA graph.
+
+    Decode batches (a few tokens) spend most of the layer's time launching its
+    ~10 kernels; a graph replays them with one launch.  The layer has no host
+    synchronisation and keeps its workspace per stream, so it captures as is.
+    ``__call__(x)`` copies x into the graph's static input, replays, and
+    returns the graph's static output (overwritten by the next replay: copy it
+    if it must outlive that).  Weights (``weights`` dict as for
+    :class:`MoePipeline`) must stay at the same addresses while the graph is
+    used."""
+
+    def __init__(self, weights: dict, T: int, *, device=None, **moe_kwargs):
+        self.w = weights
+        self.kw = moe_kwargs
+        self.dev = torch.device(device) if device is not None else weights["w13"].device
+        H = weights["w13"].shape[2]
+        self.x = torch.zeros((T, H), dtype=torch.bfloat16, device=self.dev)
+        with torch.cuda.device(self.dev):
+            # one eager call first: library load, shared-memory opt-in and
+            # other one-time set-up must not happen inside the capture
+            self._layer()
+            torch.cuda.synchronize(self.dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.y = self._layer()
+
+    def _layer(self):
+        w = self.w
+        kw = {k: w[k] for k in _SHARED if k in w}
+        kw.update(self.kw)
+        return ops.moe(self.x, w["router_w"], w["router_bias"], w["w13"], w["w13_scale"], w["w2"], w["w2_scale"],
+                       **kw)
+
+    @torch.no_grad()
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape != self.x.shape:
+            raise ValueError(f"MoeGraph was captured for x of shape {tuple(self.x.shape)}, got {tuple(x.shape)}")
+        self.x.copy_(x)
+        self.graph.replay()
+        return self.y

@@ -31,10 +31,12 @@ def test_rmsnorm_quant_matches_oracle(T, H, wdtype):
     ref = R.rmsnorm(h, wgt, 1e-6)
     yc = y.cpu()
     # The fp32 sum of squares runs in another order than torch's: the rsqrt
-    # can move by an ulp, which can flip a bf16 rounding of h * rsqrt.
+    # can move by an ulp, which can flip the bf16 rounding of h * rsqrt; the
+    # product with the weight is rounded again, so y can move by up to ~2 of
+    # its own bf16 ulps at such an element.
     diff = (yc.float() - ref.float()).abs()
     ulp = ref.float().abs().clamp_min(1e-30) * 2.0 ** -7
-    assert bool((diff <= ulp * 1.01).all()), float((diff / ulp).max())
+    assert bool((diff <= ulp * 2.01).all()), float((diff / ulp).max())
     assert float((diff > 0).double().mean()) < 1e-3
     # the quantisation is byte-exact on the kernel's own bf16 rows
     rq, rsc = R.quantize_1x128(yc)
