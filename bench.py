@@ -12,8 +12,9 @@ combine + shared expert -> bf16) over one batch of synthetic tokens.
   HBM; every step streams 11.3 GB of expert weights, far larger than the 126 MB
   L2, so no flush is needed between steps.
 * N>1 (torchrun): BASELINE config c3 -- expert parallel over N ranks, T=32768
-  tokens in total (32768/N per rank), E/N experts per rank, NCCL all-to-all
-  dispatch/combine.  Total work is fixed as N grows ("strong" scaling).
+  tokens in total (32768/N per rank), E/N experts per rank; rows exchanged
+  by NCCL all-to-all or by the device-driven exchange over symmetric memory
+  (``--ep-exchange``).  Total work is fixed as N grows ("strong" scaling).
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
 implementation of the path (the oracle restatement in ``oracle/``, bit-identical
@@ -50,8 +51,9 @@ def _args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
-    p.add_argument("--ep-combine", choices=["nccl", "peer"], default=None,
-                   help="N>1: combine through NCCL all-to-all (default) or peer reads of symmetric buffers")
+    p.add_argument("--ep-exchange", choices=["nccl", "peer"], default=None,
+                   help="N>1: rows exchanged by NCCL all-to-all or device-driven over symmetric memory "
+                        "(default: GEMMS_EP_EXCHANGE, else nccl)")
     return p.parse_args()
 
 
@@ -261,7 +263,7 @@ def config_dict(cfg, base, sh, n_local, planes, world, zipf_hist=None):
                       f"groups {sh.n_group}/{sh.topk_group} top-{sh.top_k}" + (" + shared expert" if sh.shared else "")),
          "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
          "parallelism": f"ep{world}" if world > 1 else "single GPU",
-         **({"ep_combine": os.environ.get("GEMMS_EP_COMBINE", "nccl")} if world > 1 else {}),
+         **({"ep_exchange": os.environ.get("GEMMS_EP_EXCHANGE", "nccl")} if world > 1 else {}),
          "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"}
     if zipf_hist is not None:
         per_rank = zipf_hist.reshape(8, -1).sum(1)
@@ -424,8 +426,8 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 8, 32, 128), steps=50, warmup=5):
 
 
 def gpu_arm(a):
-    if a.ep_combine:
-        os.environ["GEMMS_EP_COMBINE"] = a.ep_combine
+    if a.ep_exchange:
+        os.environ["GEMMS_EP_EXCHANGE"] = a.ep_exchange
     import torch
     import torch.distributed as dist
 
@@ -580,9 +582,10 @@ def gpu_arm(a):
             "data": "synthetic (seeded; BASELINE distributions; random-init weights)",
             "config": config_dict(cfg, base, sh, n_local, planes, world, zipf_hist),
             "tflops": tflops,
-            "fp8": {"tflops": tflops, "peak_tflops": fp8_peak, "frac": tflops / fp8_peak,
+            "fp8": {"tflops": tflops, "tflops_per_gpu": tflops / world, "peak_tflops": fp8_peak * world,
+                    "frac": tflops / (fp8_peak * world),
                     "peak_source": "measured in this run: torch._scaled_mm (cuBLAS) e4m3 8192^3, bf16 out, "
-                                   "best of 10 on this GPU"},
+                                   "best of 10 on rank 0's GPU, times the GPU count"},
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
             "e2e": e2e, "clocks": clocks}
     if decode is not None:
@@ -609,12 +612,19 @@ def gpu_arm(a):
         ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) + ep_timeline.get("shared_ffn_2", 0.0)
                                               if sh.shared else 0.0)
         ach = ffn_bytes / (ffn_ms / 1e3) / 1e9
-        line["roofline"] = {"bound": "hbm", "kernel": "grouped GEMM1+GEMM2 over received rows + shared expert "
-                                                      "(rank 0, expert_ffn + both shared_ffn phases)",
-                            "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
-                            "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else
-                            "fallback 6650 GB/s", "traffic": None, "algorithmic_bytes": ffn_bytes,
-                            "launch_ms": ffn_ms}
+        # at c3 the grouped rows per rank (>= 32k) make the FFN compute-bound:
+        # its roof is the tensor pipe (FP8 work of rank 0's grouped rows and
+        # shared rows over the same phases)
+        ffn_flops = 6.0 * H * I * (P + (sh.T if sh.shared else 0))
+        ach_tf = ffn_flops / (ffn_ms / 1e3) / 1e12
+        line["roofline"] = {"bound": "tensor", "kernel": "grouped GEMM1+GEMM2 over received rows + shared expert "
+                                                         "(rank 0, expert_ffn + shared_ffn phases)",
+                            "achieved": ach_tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": ach_tf / fp8_peak,
+                            "peak_source": "dense FP8 measured in this run (torch._scaled_mm, cuBLAS, e4m3 8192^3); "
+                                           "MEASURED_PEAKS.json has no FP8 entry",
+                            "traffic": None, "algorithmic_flops": ffn_flops, "launch_ms": ffn_ms,
+                            "hbm": {"algorithmic_bytes": ffn_bytes, "achieved_gbs": ach, "peak_gbs": hbm,
+                                    "frac": ach / hbm}}
         line["ep_timeline_ms"] = ep_timeline
     if group is None:
         ab = algorithmic_bytes(sh, counts_cpu, planes)

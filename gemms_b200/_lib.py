@@ -37,6 +37,12 @@ EXPORTS = (
     "gemms_ep_pack_back",
     "gemms_ep_combine",
     "gemms_ep_combine_rows",
+    "gemms_ep_region_bytes",
+    "gemms_ep_pull",
+    "gemms_ep_expert_ffn_dev",
+    "gemms_ep_pack_back_dev",
+    "gemms_ep_combine_peer",
+    "gemms_ep_set_pull_ctas",
     "gemms_set_gemm_ctas",
     "gemms_moe_fwd_noalloc",
     "gemms_moe_check_noalloc",
@@ -155,6 +161,23 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
                                             c_void_p, c_void_p]
         L.gemms_ep_combine_rows.restype = c_int32
         L.gemms_ep_combine.restype = c_int32
+        L.gemms_ep_region_bytes.argtypes = [c_int32, c_int32, c_int32]
+        L.gemms_ep_region_bytes.restype = c_size_t
+        L.gemms_ep_pull.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                                    c_void_p, c_void_p]
+        L.gemms_ep_pull.restype = c_int32
+        L.gemms_ep_expert_ffn_dev.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                              c_int32, c_int32, c_int32,
+                                              c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                              c_void_p]
+        L.gemms_ep_expert_ffn_dev.restype = c_int32
+        L.gemms_ep_pack_back_dev.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p]
+        L.gemms_ep_pack_back_dev.restype = c_int32
+        L.gemms_ep_combine_peer.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                            c_int32, c_void_p, c_void_p]
+        L.gemms_ep_combine_peer.restype = c_int32
+        L.gemms_ep_set_pull_ctas.argtypes = [c_int32]
+        L.gemms_ep_set_pull_ctas.restype = c_int32
         L.gemms_moe_fwd_noalloc.argtypes = [ctypes.POINTER(GemmsMoeArgs), c_void_p]
         L.gemms_moe_fwd_noalloc.restype = c_int32
         L.gemms_moe_check_noalloc.argtypes = [c_void_p, ctypes.POINTER(c_int32)]

@@ -80,8 +80,9 @@ struct AssignArgs {
   int32_t* row_token;     // [rows]
   float* row_weight;      // [rows]
   int32_t* pair_row;      // [T, top_k]
-  int shared_rows;
-  int row_capacity;       // rows at or past it are not written (plan_kernel reports the overflow)        // >0: rows offsets[E_local] + t get token t, weight 1
+  int shared_rows;         // >0: rows offsets[E_local] + t get token t, weight 1
+  int row_capacity;       // rows at or past it are not written (plan_kernel reports the overflow)
+  const int32_t* T_dev;   // when set, only tokens t < min(T, *T_dev) (a count made on the device)
 };
 int launch_assign(const AssignArgs& a, cudaStream_t s);
 
@@ -101,6 +102,7 @@ struct PermuteArgs {
   uint8_t* rows_fp8;
   float* rows_scale;
   int scale_ld;
+  const int32_t* T_dev;            // when set, only tokens t < *T_dev (a count made on the device)
 };
 int launch_permute(const PermuteArgs& a, cudaStream_t s);
 

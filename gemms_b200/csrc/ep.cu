@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 
 namespace gemms {
 namespace {
@@ -120,26 +121,30 @@ __global__ void __launch_bounds__(1024) ep_assign_kernel(const int32_t* __restri
 
 // Block (8 warps) per token: quantise once, write the token-major rows and
 // every packed send row of the token.
-__global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, 4) ep_pack_kernel(const __nv_bfloat16* __restrict__ x,
                                                       const int32_t* __restrict__ topk_idx,
                                                       const float* __restrict__ topk_w, int T, int H, int top_k,
                                                       int E_local, int world,
                                                       const int32_t* __restrict__ send_row_of,
                                                       uint8_t* __restrict__ send_buf, size_t row_bytes,
                                                       uint8_t* __restrict__ xq, float* __restrict__ xq_scale) {
+  __shared__ int s_rows[kMaxWorld];
+  __shared__ int s_dests[kMaxWorld];
+  __shared__ int s_nd;
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int rows[kMaxWorld];
-  int dests[kMaxWorld];
-  int nd = 0;
-  for (int d = 0; d < world; ++d) {
-    const int r = send_row_of[(size_t)t * world + d];
+  if (warp == 0) {  // the token's send rows, compacted in destination order
+    const int r = lane < world ? send_row_of[(size_t)t * world + lane] : -1;
+    const unsigned b = __ballot_sync(0xffffffffu, r >= 0);
     if (r >= 0) {
-      rows[nd] = r;
-      dests[nd] = d;
-      ++nd;
+      const int i = __popc(b & ((1u << lane) - 1u));
+      s_rows[i] = r;
+      s_dests[i] = lane;
     }
+    if (lane == 0) s_nd = __popc(b);
   }
+  __syncthreads();
+  const int nd = s_nd;
   const int KB = H / kBlock;
   for (int kb = warp; kb < KB; kb += 8) {
     const uint2 raw = *reinterpret_cast<const uint2*>(x + (size_t)t * H + (size_t)kb * kBlock + lane * 4);
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
     *reinterpret_cast<uint32_t*>(xq + (size_t)t * H + (size_t)kb * kBlock + lane * 4) = packed;
     if (lane == 0) xq_scale[(size_t)kb * T + t] = scale;
     for (int i = 0; i < nd; ++i) {
-      uint8_t* row = send_buf + (size_t)rows[i] * row_bytes;
+      uint8_t* row = send_buf + (size_t)s_rows[i] * row_bytes;
       *reinterpret_cast<uint32_t*>(row + (size_t)kb * kBlock + lane * 4) = packed;
       if (lane == 0) reinterpret_cast<float*>(row + H)[kb] = scale;
     }
@@ -166,12 +171,12 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
   // expert ids / weights that live on each destination
   if (warp == 0) {
     for (int i = 0; i < nd; ++i) {
-      uint8_t* row = send_buf + (size_t)rows[i] * row_bytes;
+      uint8_t* row = send_buf + (size_t)s_rows[i] * row_bytes;
       int32_t* ids = reinterpret_cast<int32_t*>(row + H + 4 * KB);
       float* ws = reinterpret_cast<float*>(row + H + 4 * KB + 4 * top_k);
       for (int j = lane; j < top_k; j += 32) {
         const int e = topk_idx[(size_t)t * top_k + j];
-        const bool here = e >= 0 && e / E_local == dests[i];
+        const bool here = e >= 0 && e / E_local == s_dests[i];
         ids[j] = here ? e : -1;
         ws[j] = here ? topk_w[(size_t)t * top_k + j] : 0.f;
       }
@@ -180,11 +185,11 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __nv_bfloat16* __res
 }
 
 // Thread per received row: local-expert histogram and pair_row = -1.
-__global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R, int H, int top_k,
-                               int local_offset, int E_local, int32_t* __restrict__ counts,
+__global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R, const int32_t* R_dev, int H,
+                               int top_k, int local_offset, int E_local, int32_t* __restrict__ counts,
                                int32_t* __restrict__ pair_row, int* err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= R) return;
+  if (r >= R || (R_dev && r >= *R_dev)) return;
   const int32_t* ids = reinterpret_cast<const int32_t*>(recv + (size_t)r * row_bytes + H + 4 * (H / kBlock));
   for (int j = 0; j < top_k; ++j) {
     pair_row[(size_t)r * top_k + j] = -1;
@@ -200,10 +205,11 @@ __global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_byte
 
 // Block per token: out[t] = bf16(acc[t] + sum of the token's returned rows).
 // Block per row: amax, then the row's values divided by 2^e as fp16.
-__global__ void __launch_bounds__(256) ep_pack_back_kernel(const float* __restrict__ rows, int H,
-                                                           uint8_t* __restrict__ packed, size_t rbb) {
+__global__ void __launch_bounds__(256) ep_pack_back_kernel(const float* __restrict__ rows, const int32_t* R_dev,
+                                                           int H, uint8_t* __restrict__ packed, size_t rbb) {
   __shared__ float s_warp[8];
   const size_t r = blockIdx.x;
+  if (R_dev && (int)r >= *R_dev) return;
   const float4* src = reinterpret_cast<const float4*>(rows + r * H);
   float amax = 0.f;
   for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
@@ -238,23 +244,39 @@ __global__ void __launch_bounds__(256) ep_pack_back_kernel(const float* __restri
 struct BackRows {
   const uint8_t* base[kMaxWorld];
   int add[kMaxWorld];
+  const int32_t* add_dev;  // when set, add[d] = add_dev[d] (offsets computed on the device)
+  int cap;                 // > 0: rows at or past it are outside the buffers and are skipped
 };
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc, const BackRows rows_at,
                                                          size_t rbb, const int32_t* __restrict__ send_row_of, int T,
                                                          int H, int world, __nv_bfloat16* __restrict__ out) {
+  __shared__ const uint8_t* s_rows[kMaxWorld];
+  __shared__ float s_scale[kMaxWorld];
+  __shared__ int s_nd;
   const int t = blockIdx.x;
-  const uint8_t* rows[kMaxWorld];
-  float scale[kMaxWorld];
-  int nd = 0;
-  for (int d = 0; d < world; ++d) {
-    const int r = send_row_of[(size_t)t * world + d];
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {  // the token's returned rows, compacted in rank order
+    const int d = lane;
+    int r = d < world ? send_row_of[(size_t)t * world + d] : -1;
+    int add = 0;
     if (r >= 0) {
-      rows[nd] = rows_at.base[d] + (size_t)(r + rows_at.add[d]) * rbb;
-      scale[nd] = *reinterpret_cast<const float*>(rows[nd] + 2 * (size_t)H);
-      ++nd;
+      add = rows_at.add_dev ? rows_at.add_dev[d] : rows_at.add[d];
+      if (rows_at.cap > 0 && (r + add < 0 || r + add >= rows_at.cap)) r = -1;  // not in the buffer: skipped
     }
+    const unsigned b = __ballot_sync(0xffffffffu, r >= 0);
+    if (r >= 0) {
+      const int i = __popc(b & ((1u << lane) - 1u));
+      const uint8_t* row = rows_at.base[d] + (size_t)(r + add) * rbb;
+      s_rows[i] = row;
+      s_scale[i] = *reinterpret_cast<const float*>(row + 2 * (size_t)H);
+    }
+    if (lane == 0) s_nd = __popc(b);
   }
+  __syncthreads();
+  const int nd = s_nd;
+  const uint8_t* const* rows = s_rows;
+  const float* scale = s_scale;
   for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
     float4 s = *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
     for (int i = 0; i < nd; ++i) {
@@ -272,6 +294,127 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
     o.y = *reinterpret_cast<uint32_t*>(&hi);
     *reinterpret_cast<uint2*>(out + (size_t)t * H + c) = o;
   }
+}
+
+// ---- device-driven exchange over symmetric (NVLink-mapped) memory ----------
+// Each rank's exchange region, allocated symmetrically so that every rank can
+// address every other rank's copy:
+//   [0, kEpHdrBytes)            int32 counts [2][world] (gemms_ep_dispatch's send_counts)
+//   [kEpHdrBytes, +send_cap*rb) send rows grouped by destination in token order
+// The receiving rank reads the counts and then its rows straight out of the
+// senders' regions (loads over NVLink): no host read of a count matrix and no
+// split sizes on the host.
+constexpr size_t kEpHdrBytes = 256;
+
+// CTAs of the row pull (0: two per SM); fewer leave SMs to a GEMM running
+// beside it on another stream.
+std::atomic<int> g_pull_ctas{0};
+int pull_ctas() { return g_pull_ctas.load(); }
+
+// Exchange plan (int32 [kEpInfoInts], device): see gemms_ep_pull in the header.
+constexpr int kInfoR = 0, kInfoP = 1, kInfoFlags = 2, kInfoStart = 8, kInfoSrcOff = 48, kInfoAdd = 88;
+
+struct PeerRegions {
+  const uint8_t* base[kMaxWorld];
+};
+
+__device__ __forceinline__ int ld_sys(const int32_t* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One warp; lane s reads source rank s's counts.  Received rows are ordered by
+// source rank, then by the source's token order (the layout an all-to-all
+// would produce).  Counts that do not fit the regions (a corrupt or foreign
+// header) set a flag and plan no rows, so no load leaves the regions.
+__global__ void ep_pull_plan_kernel(PeerRegions reg, int rank, int world, int send_cap, int recv_cap,
+                                    int32_t* __restrict__ info) {
+  const unsigned full = 0xffffffffu;
+  const int s = threadIdx.x;
+  const bool live = s < world;
+  int rows_to_me = 0, pairs_to_me = 0, my_off = 0, add = 0, flags = 0;
+  if (live) {
+    const int32_t* hdr = reinterpret_cast<const int32_t*>(reg.base[s]);
+    int sent = 0;
+    for (int d = 0; d < world; ++d) {
+      const int m = ld_sys(hdr + d);
+      if (m < 0) flags |= 2;
+      if (d < rank) my_off += m;
+      if (d == rank) rows_to_me = m;
+      sent += m;
+    }
+    pairs_to_me = ld_sys(hdr + world + rank);
+    if (sent > send_cap || pairs_to_me < 0) flags |= 2;
+    // lane d as a destination: this rank's rows for d start, in d's receive
+    // order, after the rows of ranks q < rank; in this rank's send rows they
+    // start after the rows for destinations d' < d.
+    const int32_t* mine = reinterpret_cast<const int32_t*>(reg.base[rank]);
+    int before = 0, send_off = 0;
+    for (int q = 0; q < rank; ++q) before += ld_sys(reinterpret_cast<const int32_t*>(reg.base[q]) + s);
+    for (int d = 0; d < s; ++d) send_off += ld_sys(mine + d);
+    add = before - send_off;
+  }
+  int incl = rows_to_me;
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(full, incl, off);
+    if (s >= off) incl += v;
+  }
+  int P = pairs_to_me;
+  for (int off = 16; off > 0; off >>= 1) {
+    P += __shfl_xor_sync(full, P, off);
+    flags |= __shfl_xor_sync(full, flags, off);
+  }
+  const int total = __shfl_sync(full, incl, 31);
+  if (total > recv_cap) flags |= 1;
+  const int R = flags ? 0 : total;  // nothing is pulled past a capacity or from bad counts
+  if (live) {
+    info[kInfoStart + s] = incl - rows_to_me;
+    info[kInfoSrcOff + s] = my_off;
+    info[kInfoAdd + s] = add;
+  }
+  if (s == 0) {
+    info[kInfoStart + world] = total;
+    info[kInfoR] = R;
+    info[kInfoP] = flags ? 0 : P;
+    info[kInfoFlags] = flags;
+  }
+}
+
+// Block per received row (grid-stride): 16-byte loads from the source rank's
+// region, two in flight per thread, stored into the local receive rows.
+__global__ void __launch_bounds__(256) ep_pull_rows_kernel(PeerRegions reg, const int32_t* __restrict__ info,
+                                                           int world, size_t rb, uint8_t* __restrict__ recv) {
+  __shared__ int s_start[kMaxWorld + 1];
+  __shared__ int s_off[kMaxWorld];
+  if ((int)threadIdx.x <= world) s_start[threadIdx.x] = info[kInfoStart + threadIdx.x];
+  if ((int)threadIdx.x < world) s_off[threadIdx.x] = info[kInfoSrcOff + threadIdx.x];
+  __syncthreads();
+  const int R = info[kInfoR];
+  const int n16 = static_cast<int>(rb / 16);
+  const int nt = blockDim.x;
+  for (int r = blockIdx.x; r < R; r += gridDim.x) {
+    int s = 0;
+    while (s + 1 < world && s_start[s + 1] <= r) ++s;
+    const uint4* src = reinterpret_cast<const uint4*>(reg.base[s] + kEpHdrBytes +
+                                                      (size_t)(s_off[s] + r - s_start[s]) * rb);
+    uint4* dst = reinterpret_cast<uint4*>(recv + (size_t)r * rb);
+    for (int c = threadIdx.x; c < n16; c += 2 * nt) {
+      const uint4 a = src[c];
+      const bool two = c + nt < n16;
+      uint4 b;
+      if (two) b = src[c + nt];
+      dst[c] = a;
+      if (two) dst[c + nt] = b;
+    }
+  }
+}
+
+// out[0 : *R_dev rows) = 0 (rows counted on the device).
+__global__ void ep_zero_rows_kernel(float4* __restrict__ out, const int32_t* __restrict__ R_dev, int R_cap, int H) {
+  const size_t n = (size_t)min(*R_dev, R_cap) * (H / 4);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 struct EpFfnLayout {
@@ -358,10 +501,15 @@ size_t gemms_ep_ffn_workspace_size(int32_t R_max, int32_t P_max, int32_t H, int3
   return ep_ffn_layout(R_max, P_max, H, I, E_local, top_k, planes).total;
 }
 
-int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t H, int32_t I, int32_t top_k,
-                        int32_t E_local, int32_t local_expert_offset, int32_t inter_planes, const void* w13,
-                        const float* w13_scale, const void* w2, const float* w2_scale, float* out_rows,
-                        void* workspace, size_t ws_bytes, gemms_stream_t stream_) {
+}  // extern "C"
+
+namespace {
+
+// R rows (R_dev == nullptr) or the first *R_dev of R_cap = R rows.
+int ep_expert_ffn_impl(const void* recv_buf, int32_t R, const int32_t* R_dev, int32_t P_max, int32_t H, int32_t I,
+                       int32_t top_k, int32_t E_local, int32_t local_expert_offset, int32_t inter_planes,
+                       const void* w13, const float* w13_scale, const void* w2, const float* w2_scale,
+                       float* out_rows, void* workspace, size_t ws_bytes, gemms_stream_t stream_) {
   const int planes = inter_planes == 0 ? 2 : inter_planes;
   if (R < 0 || P_max < 0 || H <= 0 || I <= 0 || E_local < 1 || H % 256 || I % kBlock || top_k < 1 || top_k > 16 ||
       planes < 2 || planes > 3)
@@ -377,9 +525,14 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t 
   const size_t rb = ep_row_bytes(H, top_k);
   const uint8_t* recv = static_cast<const uint8_t*>(recv_buf);
   GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, L.head, st));
-  GEMMS_CUDA_TRY(cudaMemsetAsync(out_rows, 0, sizeof(float) * (size_t)R * H, st));
+  if (R_dev) {
+    ep_zero_rows_kernel<<<num_sms() * 4, 256, 0, st>>>(reinterpret_cast<float4*>(out_rows), R_dev, R, H);
+    GEMMS_CUDA_TRY(cudaGetLastError());
+  } else {
+    GEMMS_CUDA_TRY(cudaMemsetAsync(out_rows, 0, sizeof(float) * (size_t)R * H, st));
+  }
   int32_t* pair_row = at<int32_t>(ws, L.pair_row);
-  ep_hist_kernel<<<cdiv(R, 256), 256, 0, st>>>(recv, rb, R, H, top_k, local_expert_offset, E_local,
+  ep_hist_kernel<<<cdiv(R, 256), 256, 0, st>>>(recv, rb, R, R_dev, H, top_k, local_expert_offset, E_local,
                                                 at<int32_t>(ws, L.counts), pair_row, err);
   GEMMS_CUDA_TRY(cudaGetLastError());
   int rc;
@@ -403,6 +556,7 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t 
   sa.topk_w = reinterpret_cast<const float*>(recv + H + 4 * KB + 4 * top_k);
   sa.idx_stride = static_cast<int>(rb / 4);
   sa.T = R;
+  sa.T_dev = R_dev;
   sa.top_k = top_k;
   sa.local_offset = local_expert_offset;
   sa.E_local = E_local;
@@ -422,6 +576,7 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t 
   qa.scale_kb_stride = 1;
   qa.scale_t_stride = static_cast<long long>(rb / 4);
   qa.T = R;
+  qa.T_dev = R_dev;
   qa.H = H;
   qa.top_k = top_k;
   qa.pair_row = pair_row;
@@ -477,6 +632,94 @@ int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t 
   return launch_gemm2(g2, st);
 }
 
+}  // namespace
+
+extern "C" {
+
+int gemms_ep_expert_ffn(const void* recv_buf, int32_t R, int32_t P_max, int32_t H, int32_t I, int32_t top_k,
+                        int32_t E_local, int32_t local_expert_offset, int32_t inter_planes, const void* w13,
+                        const float* w13_scale, const void* w2, const float* w2_scale, float* out_rows,
+                        void* workspace, size_t ws_bytes, gemms_stream_t stream) {
+  return ep_expert_ffn_impl(recv_buf, R, nullptr, P_max, H, I, top_k, E_local, local_expert_offset, inter_planes,
+                            w13, w13_scale, w2, w2_scale, out_rows, workspace, ws_bytes, stream);
+}
+
+int gemms_ep_expert_ffn_dev(const void* recv_buf, int32_t R_cap, const int32_t* info, int32_t P_max, int32_t H,
+                            int32_t I, int32_t top_k, int32_t E_local, int32_t local_expert_offset,
+                            int32_t inter_planes, const void* w13, const float* w13_scale, const void* w2,
+                            const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
+                            gemms_stream_t stream) {
+  if (!info) return GEMMS_ERR_ARG;
+  return ep_expert_ffn_impl(recv_buf, R_cap, info + kInfoR, P_max, H, I, top_k, E_local, local_expert_offset,
+                            inter_planes, w13, w13_scale, w2, w2_scale, out_rows, workspace, ws_bytes, stream);
+}
+
+size_t gemms_ep_region_bytes(int32_t send_cap, int32_t H, int32_t top_k) {
+  if (send_cap < 0 || H <= 0 || H % kBlock || top_k < 1 || top_k > 16) return 0;
+  return kEpHdrBytes + (size_t)send_cap * ep_row_bytes(H, top_k);
+}
+
+int gemms_ep_pull(const void* const* region, int32_t rank, int32_t world, int32_t H, int32_t top_k,
+                  int32_t send_cap, int32_t recv_cap, void* recv_buf, int32_t* info, gemms_stream_t stream_) {
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || H <= 0 || H % kBlock || top_k < 1 ||
+      top_k > 16 || send_cap < 0 || recv_cap < 0)
+    return GEMMS_ERR_SHAPE;
+  if (!region || !info || (!recv_buf && recv_cap > 0)) return GEMMS_ERR_ARG;
+  if ((recv_buf && !aligned16(recv_buf)) || (reinterpret_cast<uintptr_t>(info) & 3u)) return GEMMS_ERR_ALIGN;
+  PeerRegions reg{};
+  for (int s = 0; s < world; ++s) {
+    if (!region[s]) return GEMMS_ERR_ARG;
+    if (!aligned16(region[s])) return GEMMS_ERR_ALIGN;
+    reg.base[s] = static_cast<const uint8_t*>(region[s]);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
+  ep_pull_plan_kernel<<<1, 32, 0, st>>>(reg, rank, world, send_cap, recv_cap, info);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  if (recv_cap == 0) return GEMMS_OK;
+  const int blocks = std::min(recv_cap, pull_ctas() > 0 ? pull_ctas() : num_sms() * 2);
+  ep_pull_rows_kernel<<<blocks, 256, 0, st>>>(reg, info, world, ep_row_bytes(H, top_k),
+                                               static_cast<uint8_t*>(recv_buf));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_ep_pack_back_dev(const float* rows, int32_t R_cap, const int32_t* info, int32_t H, void* packed,
+                           gemms_stream_t stream_) {
+  if (R_cap < 0 || H <= 0 || H % 4) return GEMMS_ERR_SHAPE;
+  if (R_cap == 0) return GEMMS_OK;
+  if (!rows || !packed || !info) return GEMMS_ERR_ARG;
+  if (!aligned16(rows) || !aligned16(packed)) return GEMMS_ERR_ALIGN;
+  ep_pack_back_kernel<<<R_cap, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      rows, info + kInfoR, H, static_cast<uint8_t*>(packed), ep_back_row_bytes(H));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_ep_combine_peer(const float* acc, const void* const* row_base, const int32_t* info,
+                          const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, int32_t recv_cap,
+                          void* out_bf16, gemms_stream_t stream_) {
+  if (T < 0 || H <= 0 || H % 4 || world < 1 || world > kMaxWorld || recv_cap < 1) return GEMMS_ERR_SHAPE;
+  if (!acc || !send_row_of || !out_bf16 || !row_base || !info) return GEMMS_ERR_ARG;
+  if (!aligned16(acc) || !aligned16(out_bf16)) return GEMMS_ERR_ALIGN;
+  if (T == 0) return GEMMS_OK;
+  BackRows at{};
+  for (int d = 0; d < world; ++d) {
+    if (row_base[d] && !aligned16(row_base[d])) return GEMMS_ERR_ALIGN;
+    at.base[d] = static_cast<const uint8_t*>(row_base[d]);
+  }
+  at.add_dev = info + kInfoAdd;
+  at.cap = recv_cap;
+  ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_ep_set_pull_ctas(int32_t ctas) {
+  if (ctas < 0) return GEMMS_ERR_ARG;
+  return g_pull_ctas.exchange(ctas);
+}
+
 size_t gemms_ep_back_row_bytes(int32_t H) { return H > 0 ? ep_back_row_bytes(H) : 0; }
 
 int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, gemms_stream_t stream_) {
@@ -485,7 +728,7 @@ int gemms_ep_pack_back(const float* rows, int32_t R, int32_t H, void* packed, ge
   if (!rows || !packed) return GEMMS_ERR_ARG;
   if (!aligned16(rows) || !aligned16(packed)) return GEMMS_ERR_ALIGN;
   ep_pack_back_kernel<<<R, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      rows, H, static_cast<uint8_t*>(packed), ep_back_row_bytes(H));
+      rows, nullptr, H, static_cast<uint8_t*>(packed), ep_back_row_bytes(H));
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

@@ -27,16 +27,25 @@ __device__ __forceinline__ uint32_t quant4(float v0, float v1, float v2, float v
 // Each lane owns 4 consecutive columns of a block, so a warp writes one
 // 128-byte line per destination row.
 __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a) {
+  constexpr int kMaxDst = 17;  // top_k <= 16 + the shared expert
+  __shared__ int s_dst[kMaxDst];
+  __shared__ int s_nd;
   const int t = blockIdx.x;
+  if (a.T_dev && t >= *a.T_dev) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kMaxDst = 17;
-  int dst[kMaxDst];
-  int nd = 0;
-  for (int j = 0; j < a.top_k; ++j) {
-    const int r = a.pair_row[(size_t)t * a.top_k + j];
-    if (r >= 0) dst[nd++] = r;
+  if (warp == 0) {  // the token's grouped rows, compacted in slot order
+    const int r = lane < a.top_k ? a.pair_row[(size_t)t * a.top_k + lane] : -1;
+    const unsigned b = __ballot_sync(0xffffffffu, r >= 0);
+    if (r >= 0) s_dst[__popc(b & ((1u << lane) - 1u))] = r;
+    int nd = __popc(b);
+    if (lane == 0) {
+      if (a.shared_row0) s_dst[nd++] = *a.shared_row0 + t;
+      s_nd = nd;
+    }
   }
-  if (a.shared_row0) dst[nd++] = *a.shared_row0 + t;
+  __syncthreads();
+  const int nd = s_nd;
+  const int* dst = s_dst;
   if (nd == 0) return;
   const int KB = a.H / kBlock;
   for (int kb = warp; kb < KB; kb += 8) {

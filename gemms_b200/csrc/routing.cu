@@ -230,9 +230,10 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
   const int le = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = blockDim.x >> 5;
+  const int T = a.T_dev ? min(a.T, *a.T_dev) : a.T;
   if (le == a.E_local) {  // shared expert group: row offsets[E_local] + t
     const int r0 = a.offsets[a.E_local];
-    for (int t = tid; t < a.T && r0 + t < a.row_capacity; t += blockDim.x) {
+    for (int t = tid; t < T && r0 + t < a.row_capacity; t += blockDim.x) {
       a.row_token[r0 + t] = t;
       a.row_weight[r0 + t] = 1.0f;
     }
@@ -242,10 +243,10 @@ __global__ void __launch_bounds__(1024) assign_kernel(AssignArgs a) {
   const int stride = a.idx_stride > 0 ? a.idx_stride : a.top_k;
   if (tid == 0) s_base = a.offsets[le];
   __syncthreads();
-  for (int t0 = 0; t0 < a.T; t0 += blockDim.x) {
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
     const int t = t0 + tid;
     int jsel = -1;
-    if (t < a.T) {
+    if (t < T) {
       for (int j = 0; j < a.top_k; ++j)
         if (a.topk_idx[(size_t)t * stride + j] == ge) jsel = j;
     }

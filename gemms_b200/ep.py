@@ -12,20 +12,29 @@ expert are replicated.  One layer forward on every rank:
    groups align with ranks, e.g. EP8 of DeepSeek-V3), rows grouped by
    destination in token order, quantised per 1x128 and packed with the ids and
    weights of the experts on the destination;
-3. count exchange (``all_gather`` of each rank's per-destination row counts,
-   then one host read of the count matrix) and the dispatch
-   ``all_to_all_single`` of packed rows -- the shared expert runs on the first
-   half of the rank's own tokens meanwhile (all of them with the peer
-   combine);
+3. the exchange of the packed rows, in one of two modes:
+
+   * ``"nccl"``: an ``all_gather`` of each rank's per-destination counts, one
+     host read of the count matrix (split sizes), and ``all_to_all_single``
+     of the rows; the shared expert runs on the first half of the rank's own
+     tokens meanwhile;
+   * ``"peer"`` (device-driven, no host synchronisation): each rank writes its
+     counts and rows into its own exchange region, a symmetric allocation that
+     every rank can address over NVLink; after one barrier each rank's pull
+     kernel reads all ranks' counts and copies the rows sent to it straight
+     from the senders' regions.  Buffers are sized by capacities
+     (``max_tokens_per_rank``), so nothing about the counts is needed on the
+     host and the whole layer can be captured in a CUDA graph;
+
 4. grouped GEMMs over the received rows, each row's result pre-reduced over its
    local experts in fp32;
 5. the rows go back as fp16 with a per-row power-of-two scale (exact
-   scaling, half the bytes of fp32), ``all_to_all_single`` while the shared
-   expert runs on the second half of the tokens, and a deterministic
-   gather-sum per token plus the shared expert, cast to bf16.  With the peer
-   combine (``combine="peer"``) the packed rows instead stay in a symmetric
-   buffer on the rank that computed them and, after one barrier, the gather
-   reads them from there over NVLink.
+   scaling, half the bytes of fp32): ``"nccl"`` sends them with
+   ``all_to_all_single`` while the shared expert runs on the second half of
+   the tokens; ``"peer"`` leaves them in the exchange region of the rank that
+   computed them and, after a second barrier, the token's own rank reads them
+   from there.  A deterministic gather-sum per token plus the shared expert,
+   cast to bf16, ends the layer.
 
 Every rank issues the same collectives in the same order.  The device work
 goes through a ``kernels`` object: :class:`CudaEpKernels` (the C ABI) by
@@ -54,6 +63,14 @@ def row_bytes(H: int, top_k: int) -> int:
 def back_row_bytes(H: int) -> int:
     """Bytes of one packed combine row (``gemms_ep_back_row_bytes``): fp16 [H] + fp32 2^e."""
     return (2 * H + 4 + 15) // 16 * 16
+
+
+class _Region:
+    """A rank's exchange region and the local buffers that go with it: ``hdr``
+    (int32 [2, world] counts), ``send`` (packed send rows), ``back`` (packed
+    combine rows), ``bases`` / ``back_bases`` (every rank's address of its
+    region / of its combine rows), ``recv`` and ``info`` (this rank's received
+    rows and exchange plan), ``send_cap`` / ``recv_cap`` (rows)."""
 
 
 class CudaEpKernels:
@@ -101,14 +118,19 @@ class CudaEpKernels:
                           routed_scaling_factor=rsf, counts=False)
         return idx, w
 
-    def dispatch(self, idx, w, x, world: int, E_local: int):
+    def dispatch(self, idx, w, x, world: int, E_local: int, region=None):
+        """Packed send rows and counts; into ``region``'s header and send rows
+        (device-driven exchange) when given."""
         T, H = x.shape
         k = idx.shape[1]
         dev = x.device
         rb = row_bytes(H, k)
-        send_counts = torch.empty((2, world), dtype=torch.int32, device=dev)  # rows, pairs per destination
+        if region is not None:
+            send_counts, send_buf = region.hdr, region.send
+        else:
+            send_counts = torch.empty((2, world), dtype=torch.int32, device=dev)  # rows, pairs per destination
+            send_buf = torch.empty((max(T * min(world, k), 1), rb), dtype=torch.uint8, device=dev)
         send_row_of = torch.empty((T, world), dtype=torch.int32, device=dev)
-        send_buf = torch.empty((max(T * min(world, k), 1), rb), dtype=torch.uint8, device=dev)
         xq = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
         xq_scale = torch.empty((H // BLOCK, T), dtype=torch.float32, device=dev)
         _lib.check(self.L.gemms_ep_dispatch(idx.data_ptr(), w.data_ptr(), x.data_ptr(), T, H, k, world, E_local,
@@ -166,55 +188,110 @@ class CudaEpKernels:
                    "gemms_ep_pack_back")
         return packed[:R]
 
-    # ---- peer-memory combine (GEMMS_EP_COMBINE=peer) --------------------
-    def peer_buffers(self, group, cap_rows: int, H: int):
-        """This rank's half of a double-buffered symmetric allocation for packed
-        combine rows and every rank's address of it (peer pointers, mapped into
-        this process).  Calls alternate between the two buffers: a rank writes
-        buffer i % 2 only after the barrier of call i - 1, which every rank
-        passes only once it has finished reading buffer (i - 2) % 2.  Grows
-        (collectively: ``cap_rows`` is the same on every rank) when needed."""
+    # ---- device-driven exchange (exchange="peer") ------------------------
+    def exchange_region(self, group, send_cap: int, recv_cap: int, H: int, top_k: int):
+        """This rank's exchange region (a symmetric allocation: the header of
+        counts, ``send_cap`` packed send rows, ``recv_cap`` packed combine rows)
+        with every rank's address of it, and the local receive buffers.
+
+        Collective when it (re)allocates: every rank must pass the same
+        capacities (they follow from ``max_tokens_per_rank``).  One region
+        per group serves every call: a rank rewrites its send rows only after
+        the combine barrier of the previous call, which no rank passes before
+        it has pulled its rows, and its combine rows only after the dispatch
+        barrier of this call, which no rank passes before it has finished the
+        previous combine."""
         import torch.distributed._symmetric_memory as symm_mem
         g = group if group is not None else dist.group.WORLD
-        rbb = back_row_bytes(H)
-        need = max(cap_rows, 1) * rbb
-        st = self._symm.get(g.group_name)
-        if st is None or st["bytes"] < need:
-            if st is not None:  # peers may still read the old buffers: barrier, then drain before freeing
-                self.peer_publish(g, None, None)
+        world = dist.get_world_size(g)
+        rb, rbb = row_bytes(H, top_k), back_row_bytes(H)
+        send_bytes = self.L.gemms_ep_region_bytes(send_cap, H, top_k)
+        if send_bytes == 0:
+            raise ValueError("unsupported expert-parallel exchange geometry")
+        back_off = -(-send_bytes // 256) * 256
+        need = back_off + max(recv_cap, 1) * rbb
+        key = (g.group_name, H, top_k)
+        st = self._symm.get(key)
+        if st is None or st.nbytes < need or st.send_cap < send_cap or st.recv_cap < recv_cap:
+            if st is not None:  # peers may still read the old region: barrier, then drain before freeing
+                self.peer_barrier(g, st)
                 torch.cuda.current_stream().synchronize()
             nbytes = -(-need * 5 // 4 // (1 << 20)) * (1 << 20)  # 25% headroom, whole MiB
             dev = torch.device("cuda", torch.cuda.current_device())
-            bufs, ptrs, hdls = [], [], []
-            for _ in range(2):
-                b = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
-                h = symm_mem.rendezvous(b, g)
-                bufs.append(b)
-                hdls.append(h)
-                ptrs.append([int(p) for p in h.buffer_ptrs])
-            st = {"bytes": nbytes, "bufs": bufs, "ptrs": ptrs, "hdls": hdls, "parity": 0}
-            self._symm[g.group_name] = st
-        i = st["parity"]
-        st["parity"] ^= 1
-        return st["bufs"][i], st["ptrs"][i]
+            buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+            hdl = symm_mem.rendezvous(buf, g)
+            st = _Region()
+            st.buf, st.hdl, st.nbytes = buf, hdl, nbytes
+            st.bases = [int(p) for p in hdl.buffer_ptrs]
+            st.world, st.rb, st.rbb, st.back_off = world, rb, rbb, back_off
+            st.send_cap = (back_off - 256) // rb          # >= send_cap
+            st.recv_cap = (nbytes - back_off) // rbb      # >= recv_cap (the headroom lands here)
+            st.hdr = buf[:8 * world].view(torch.int32).view(2, world)
+            st.send = buf[256:256 + st.send_cap * rb].view(st.send_cap, rb)
+            st.back = buf[back_off:back_off + st.recv_cap * rbb]
+            st.back_bases = [b + back_off for b in st.bases]
+            st.recv = torch.empty((max(st.recv_cap, 1), rb), dtype=torch.uint8, device=dev)
+            st.info = torch.zeros(128, dtype=torch.int32, device=dev)
+            st.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+            self._symm[key] = st
+        return st
 
-    def peer_publish(self, group, local, peers):
-        """Barrier: every rank's writes of its buffer are complete (a one-element
-        NCCL all-reduce, ordered after them on each rank's stream)."""
-        tok = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
-        dist.all_reduce(tok, group=group)
-        return peers
+    def peer_barrier(self, group, region):
+        """Every rank's writes before this point (on its current stream) are
+        complete before any rank's work after it: a one-element NCCL
+        all-reduce, ordered on each rank's stream after the writes."""
+        dist.all_reduce(region.tok, group=group)
 
-    def combine_rows(self, acc, peers, row_add, send_row_of, world: int):
-        """out bf16 [T, H] = acc + the packed rows read in place from each
-        destination's buffer (``gemms_ep_combine_rows``)."""
+    def pull(self, region, rank: int, world: int, H: int, top_k: int):
+        """Rows sent to this rank -> region.recv [recv_cap, row_bytes] and the
+        exchange plan region.info (``gemms_ep_pull``)."""
+        bases = (ctypes.c_void_p * world)(*region.bases)
+        _lib.check(self.L.gemms_ep_pull(bases, rank, world, H, top_k, region.send_cap, region.recv_cap,
+                                        region.recv.data_ptr(), region.info.data_ptr(), self._stream()),
+                   "gemms_ep_pull")
+        return region.recv, region.info
+
+    def expert_ffn_dev(self, recv_buf, info, R_cap: int, P_cap: int, H: int, I: int, top_k: int, E_local: int,
+                       offset: int, planes: int, w13, w13_scale, w2, w2_scale):
+        """As expert_ffn over the first info[0] of R_cap received rows (count
+        read on the device) -> fp32 [R_cap, H]."""
+        dev = w13.device
+        key = (dev.index, torch.cuda.current_stream(dev).cuda_stream, "ep_rows")
+        out = self._ws.get(key)
+        if out is None or out.shape[0] < max(R_cap, 1) or out.shape[1] != H:
+            out = torch.empty((max(R_cap, 1), H), dtype=torch.float32, device=dev)
+            self._ws[key] = out
+        nbytes = self.L.gemms_ep_ffn_workspace_size(R_cap, P_cap, H, I, E_local, top_k, planes)
+        if nbytes == 0:
+            raise ValueError("unsupported expert-parallel FFN geometry")
+        ws = self._workspace(dev, nbytes, "ep_ffn")
+        _lib.check(self.L.gemms_ep_expert_ffn_dev(recv_buf.data_ptr(), R_cap, info.data_ptr(), P_cap, H, I, top_k,
+                                                  E_local, offset, planes, w13.data_ptr(), w13_scale.data_ptr(),
+                                                  w2.data_ptr(), w2_scale.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                                  nbytes, self._stream()), "gemms_ep_expert_ffn_dev")
+        self._ffn_ws = ws
+        return out[:max(R_cap, 1)]
+
+    def pack_back_dev(self, rows, info, region):
+        """The first info[0] result rows -> packed combine rows in region.back."""
+        R_cap, H = rows.shape
+        _lib.check(self.L.gemms_ep_pack_back_dev(rows.data_ptr(), min(R_cap, region.recv_cap), info.data_ptr(), H,
+                                                 region.back.data_ptr(), self._stream()), "gemms_ep_pack_back_dev")
+
+    def combine_peer(self, acc, region, info, send_row_of, world: int):
+        """out bf16 [T, H] = acc + this rank's combine rows read in place from
+        every destination's region (``gemms_ep_combine_peer``)."""
         T, H = acc.shape
         out = torch.empty((T, H), dtype=torch.bfloat16, device=acc.device)
-        bases = (ctypes.c_void_p * world)(*peers)
-        adds = (ctypes.c_int32 * world)(*row_add)
-        _lib.check(self.L.gemms_ep_combine_rows(acc.data_ptr(), bases, adds, send_row_of.data_ptr(), T, H, world,
-                                                out.data_ptr(), self._stream()), "gemms_ep_combine_rows")
+        bases = (ctypes.c_void_p * world)(*region.back_bases)
+        _lib.check(self.L.gemms_ep_combine_peer(acc.data_ptr(), bases, info.data_ptr(), send_row_of.data_ptr(), T, H,
+                                                world, region.recv_cap, out.data_ptr(), self._stream()),
+                   "gemms_ep_combine_peer")
         return out
+
+    def exchange_flags(self, region) -> int:
+        """info[2] of the last pull (reads the device: synchronises)."""
+        return int(region.info[2].item())
 
     def combine(self, acc, back, send_row_of, world: int):
         T, H = acc.shape
@@ -238,7 +315,8 @@ def _cuda_kernels() -> CudaEpKernels:
 @torch.no_grad()
 def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13=None, shared_w13_scale=None,
            shared_w2=None, shared_w2_scale=None, n_group=8, topk_group=4, top_k=8, routed_scaling_factor=2.5,
-           inter_planes=2, logits=None, group=None, kernels=None, timeline=None, combine=None):
+           inter_planes=2, logits=None, group=None, kernels=None, timeline=None, exchange=None,
+           max_tokens_per_rank=None):
     """Expert-parallel layer forward on this rank's tokens ``x`` [T_r, H].
 
     ``w13``/``w2`` (and scales) hold this rank's ``E/W`` experts; the rank's
@@ -246,13 +324,15 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     ``(phase, torch.cuda.Event)`` pairs recorded on the current stream at the
     phase boundaries, for per-phase device timing, and the counts
     ``("recv_rows", R)``, ``("pair_rows", P)`` (grouped-GEMM rows: received
-    rows times the local experts each names) and ``("experts_hit", n)``.
+    rows times the local experts each names) and ``("experts_hit", n)``
+    (read from the device after the last phase).
 
-    ``combine`` (default: ``GEMMS_EP_COMBINE``, else ``"nccl"``) picks how the
-    result rows come back: ``"nccl"`` sends them with ``all_to_all_single``;
-    ``"peer"`` leaves them in a symmetric (NVLink-mapped) buffer on the rank
-    that computed them and the combine kernel of the token's own rank reads
-    them from there, after one barrier.
+    ``exchange`` (default: ``GEMMS_EP_EXCHANGE``, else ``"nccl"``) picks how
+    rows travel: ``"nccl"`` (count exchange read on the host, then
+    ``all_to_all_single`` both ways) or ``"peer"`` (device-driven over
+    symmetric memory, no host synchronisation; every rank must pass the same
+    ``T_r``, or the same ``max_tokens_per_rank`` >= its ``T_r``, which sizes
+    the exchange buffers).
     """
     def mark(name):
         if timeline is not None:
@@ -261,9 +341,9 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
             timeline.append((name, ev))
 
     mark("start")
-    combine = combine or os.environ.get("GEMMS_EP_COMBINE", "nccl")
-    if combine not in ("nccl", "peer"):
-        raise ValueError(f"combine must be 'nccl' or 'peer', not {combine!r}")
+    exchange = exchange or os.environ.get("GEMMS_EP_EXCHANGE", "nccl")
+    if exchange not in ("nccl", "peer"):
+        raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
     K = kernels if kernels is not None else _cuda_kernels()
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -273,72 +353,48 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
         raise ValueError(f"each rank must hold E/world experts: E={E}, world={world}, local={E_local}")
     T, H = x.shape
     I = w13.shape[1] // 2
+    T_cap = T if max_tokens_per_rank is None else int(max_tokens_per_rank)
+    if T > T_cap:
+        raise ValueError(f"{T} tokens on this rank exceed max_tokens_per_rank={T_cap}")
     if logits is None:
         logits = K.router_logits(x, router_w)
     idx, wts = K.route(logits, router_bias, n_group, topk_group, top_k, routed_scaling_factor)
     mark("router")
+    shared = (shared_w13, shared_w13_scale, shared_w2, shared_w2_scale)
+    if exchange == "peer":
+        return _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, world, rank, E_local, T_cap,
+                            H, I, top_k, inter_planes, mark, timeline)
+
     send_counts, send_row_of, send_buf, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local)
     mark("pack")
-
     # count matrices on every rank: m[src][dst] rows and mp[src][dst] routed
-    # pairs -- this rank's send and receive counts, the size of its grouped
-    # rows, and (peer combine) where its rows sit in each destination's order
+    # pairs -- this rank's send and receive counts and the size of its grouped rows
     gathered = [torch.empty_like(send_counts) for _ in range(world)]
     dist.all_gather(gathered, send_counts, group=group)
-    both = torch.stack(gathered).cpu().tolist()  # the one host synchronisation of the layer
+    both = torch.stack(gathered).cpu().tolist()  # the one host synchronisation of this mode
     m = [b[0] for b in both]
     sc = [int(v) for v in m[rank]]
     rc = [int(m[src][rank]) for src in range(world)]
     S, R = sum(sc), sum(rc)
     P = sum(int(b[1][rank]) for b in both)
     mark("count_exchange")
-    if timeline is not None:
-        timeline.append(("recv_rows", R))
     rb = send_buf.shape[1]
     recv_buf = torch.empty((R, rb), dtype=torch.uint8, device=send_buf.device)
     work = dist.all_to_all_single(recv_buf, send_buf[:S].contiguous(), rc, sc, group=group, async_op=True)
 
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
-    # With the all-to-all combine the shared expert is split so that its second
-    # half hides that collective; the peer combine has no collective to hide.
-    T1 = T // 2 if combine == "nccl" else T
-    shared = (shared_w13, shared_w13_scale, shared_w2, shared_w2_scale)
+    # the shared expert is split so that its halves hide the two all-to-alls
+    T1 = T // 2
     if shared_w13 is not None:  # first half of the tokens overlaps the dispatch all-to-all
         with K.comm_overlap():
             K.shared_ffn(xq[:T1], xq_scale[:, :T1], *shared, inter_planes, acc, 0)
     mark("shared_ffn")
     work.wait()
     mark("dispatch_wait")
-    stats = None
-    if timeline is not None and R > 0:
-        # grouped-GEMM rows (one per received row and local expert it names)
-        # and local experts hit, for a roofline byte count; counted on the
-        # device now, read on the host after the last mark
-        off = H + 4 * (H // BLOCK)
-        ids = recv_buf[:R, off:off + 4 * top_k].contiguous().view(torch.int32)
-        le = ids.to(torch.int64) - rank * E_local
-        valid = (ids >= 0) & (le >= 0) & (le < E_local)
-        slot = torch.where(valid, le, torch.full_like(le, E_local)).flatten()  # no host sync (unlike masks)
-        per_expert = torch.zeros(E_local + 1, dtype=torch.int64, device=ids.device)
-        per_expert.scatter_add_(0, slot, torch.ones_like(slot))
-        stats = (valid.sum(), per_expert[:E_local])
-
+    stats = _recv_stats(recv_buf, R, H, top_k, rank, E_local) if timeline is not None else None
     out_rows = K.expert_ffn(recv_buf, R, P, H, I, top_k, E_local, rank * E_local, inter_planes,
                             w13, w13_scale, w2, w2_scale)
     mark("expert_ffn")
-    if combine == "peer":
-        send_off = [sum(sc[:d]) for d in range(world)]
-        row_add = [sum(int(m[src][d]) for src in range(rank)) - send_off[d] for d in range(world)]
-        cap = max(sum(int(m[src][d]) for src in range(world)) for d in range(world))
-        local, peers = K.peer_buffers(group, cap, H)
-        K.pack_back(out_rows, out=local)
-        mark("pack_back")
-        peers = K.peer_publish(group, local, peers)
-        mark("publish")
-        out = K.combine_rows(acc, peers, row_add, send_row_of, world)
-        mark("gather")
-        _timeline_stats(timeline, stats)
-        return out
     packed = K.pack_back(out_rows)
     mark("pack_back")
     back = torch.empty((S, packed.shape[1]), dtype=torch.uint8, device=x.device)
@@ -355,9 +411,66 @@ def moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, *, shared_w13
     return out
 
 
+def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, world, rank, E_local, T_cap, H, I,
+                 top_k, inter_planes, mark, timeline):
+    """exchange="peer": the layer after routing with the device-driven
+    exchange.  Two barriers per call (after the dispatch, after the result
+    rows are packed) and no host read of any count: buffers are sized by
+    capacities (received rows <= world * T_cap, grouped pairs <= received
+    rows * min(top_k, E_local)); counts beyond them raise the plan's flag
+    and nothing is copied (``exchange_flags``)."""
+    T = x.shape[0]
+    send_cap = max(T_cap * min(world, top_k), 1)
+    recv_cap = max(T_cap * world, 1)
+    P_cap = recv_cap * min(top_k, E_local)
+    reg = K.exchange_region(group, send_cap, recv_cap, H, top_k)
+    send_counts, send_row_of, _, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local, region=reg)
+    mark("pack")
+    K.peer_barrier(group, reg)  # every rank's counts and send rows are written
+    mark("publish_rows")
+    recv_buf, info = K.pull(reg, rank, world, H, top_k)
+    mark("pull")
+    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
+    if shared[0] is not None:
+        K.shared_ffn(xq, xq_scale, *shared, inter_planes, acc, 0)
+    mark("shared_ffn")
+    stats = _recv_stats(recv_buf, info, H, top_k, rank, E_local) if timeline is not None else None
+    out_rows = K.expert_ffn_dev(recv_buf, info, reg.recv_cap, P_cap, H, I, top_k, E_local, rank * E_local,
+                                inter_planes, w13, w13_scale, w2, w2_scale)
+    mark("expert_ffn")
+    K.pack_back_dev(out_rows, info, reg)
+    mark("pack_back")
+    K.peer_barrier(group, reg)  # every rank's combine rows are written
+    mark("publish")
+    out = K.combine_peer(acc, reg, info, send_row_of, world)
+    mark("gather")
+    _timeline_stats(timeline, stats)
+    return out
+
+
+def _recv_stats(recv_buf, R, H, top_k, rank, E_local):
+    """Received rows, grouped-GEMM rows (one per received row and local expert
+    it names) and local experts hit, as device tensors (no synchronisation;
+    read after the timed phases).  R is an int or the exchange plan (info[0])."""
+    n = recv_buf.shape[0]
+    if n == 0:
+        return None
+    off = H + 4 * (H // BLOCK)
+    ids = recv_buf[:, off:off + 4 * top_k].contiguous().view(torch.int32)
+    R_t = R[0] if torch.is_tensor(R) else torch.tensor(R, device=recv_buf.device)
+    live = (torch.arange(n, device=recv_buf.device) < R_t).unsqueeze(1)
+    le = ids.to(torch.int64) - rank * E_local
+    valid = live & (ids >= 0) & (le >= 0) & (le < E_local)
+    slot = torch.where(valid, le, torch.full_like(le, E_local)).flatten()
+    per_expert = torch.zeros(E_local + 1, dtype=torch.int64, device=ids.device)
+    per_expert.scatter_add_(0, slot, torch.ones_like(slot))
+    return R_t, valid.sum(), per_expert[:E_local]
+
+
 def _timeline_stats(timeline, stats):
     if timeline is None:
         return
-    pairs, per_expert = (0, None) if stats is None else (int(stats[0]), stats[1])
+    R, pairs, per_expert = (0, 0, None) if stats is None else (int(stats[0]), int(stats[1]), stats[2])
+    timeline.append(("recv_rows", R))
     timeline.append(("pair_rows", pairs))
     timeline.append(("experts_hit", 0 if per_expert is None else int((per_expert > 0).sum())))

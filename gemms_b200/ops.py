@@ -211,14 +211,18 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         shared_w2: torch.Tensor | None = None, shared_w2_scale: torch.Tensor | None = None,
         n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
         inter_planes: int = 2, logits: torch.Tensor | None = None, ep_group=None,
-        return_routing: bool = False, profile_events=None, residual: torch.Tensor | None = None):
+        return_routing: bool = False, profile_events=None, residual: torch.Tensor | None = None,
+        ep_exchange: str | None = None, max_tokens_per_rank: int | None = None):
     """DeepSeek-V3 MoE layer forward: bf16 x [T, H] -> bf16 [T, H].
 
     ``w13`` [E, 2I, H] / ``w2`` [E, H, I] are e4m3 with fp32 128x128 block
     scales; ``router_w`` fp32 [E, H], ``router_bias`` [E].  With ``ep_group``
     (a torch.distributed process group) the weights passed are this rank's
-    E/world experts and tokens are exchanged with NCCL all-to-all.
-    ``logits`` overrides the router GEMM.  ``profile_events`` (three recorded
+    E/world experts and tokens are exchanged between the ranks:
+    ``ep_exchange="nccl"`` (NCCL all-to-all, split sizes read on the host) or
+    ``"peer"`` (device-driven over symmetric memory, no host synchronisation;
+    every rank passes the same T or ``max_tokens_per_rank``); the default is
+    ``GEMMS_EP_EXCHANGE``, else ``"nccl"``.  ``logits`` overrides the router GEMM.  ``profile_events`` (three recorded
     ``torch.cuda.Event``) brackets GEMM1 and GEMM2 for kernel timing.
     ``residual`` (bf16 [T, H]) is added to the layer's fp32 result before the
     single rounding to bf16 (the decoder's residual add, fused).
@@ -231,7 +235,8 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
                          shared_w13_scale=shared_w13_scale, shared_w2=shared_w2, shared_w2_scale=shared_w2_scale,
                          n_group=n_group, topk_group=topk_group, top_k=top_k,
                          routed_scaling_factor=routed_scaling_factor, inter_planes=inter_planes,
-                         logits=logits, group=ep_group)
+                         logits=logits, group=ep_group, exchange=ep_exchange,
+                         max_tokens_per_rank=max_tokens_per_rank)
     has_shared = shared_w13 is not None
     dev = _check_cuda(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13, shared_w13_scale,
                       shared_w2, shared_w2_scale, logits, residual)

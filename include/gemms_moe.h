@@ -240,6 +240,60 @@ int gemms_ep_combine_rows(const float* acc, const void* const* row_base, const i
                           const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, void* out_bf16,
                           gemms_stream_t stream);
 
+/* ---- device-driven exchange (no host read of counts) ----
+ * Replaces the count exchange and the dispatch all-to-all: every rank owns an
+ * exchange region in memory that all ranks can address (a symmetric
+ * allocation; its peer pointers are read over NVLink):
+ *   [0, 256)    int32 counts [2][world], written by gemms_ep_dispatch as its
+ *               send_counts
+ *   [256, ...)  send rows [send_cap, row_bytes], gemms_ep_dispatch's send_buf
+ * gemms_ep_region_bytes gives the size.  After a barrier that orders every
+ * rank's dispatch before this call, gemms_ep_pull reads all ranks' counts and
+ * copies the rows sent to `rank` from their regions into recv_buf
+ * [recv_cap, row_bytes] (received rows ordered by source rank, then by the
+ * source's token order), and writes the plan to info (int32 [128], device):
+ *   info[0]       R, rows received (0 when a flag is set)
+ *   info[1]       P, routed (row, local expert) pairs they carry
+ *   info[2]       flags: 1 = more than recv_cap rows were sent to this rank,
+ *                 2 = a region's counts exceed send_cap or are negative;
+ *                 nothing is copied when set
+ *   info[8 + s]   first received row from rank s (s = 0..world)
+ *   info[48 + s]  where this rank's rows start among rank s's send rows
+ *   info[88 + d]  offset for gemms_ep_combine_peer: this rank's combine row
+ *                 for (t, d) is row send_row_of[t, d] + info[88 + d] of d's
+ *                 packed combine rows
+ * region[s] are the `world` region addresses (host array).  The caller keeps
+ * every region unwritten until all ranks' pulls of this call have completed.
+ * No counterpart in the reference (its only distributed hook is
+ * local_expert_offset, flashinfer_baseline.py:132-138). */
+size_t gemms_ep_region_bytes(int32_t send_cap, int32_t H, int32_t top_k);
+int gemms_ep_pull(const void* const* region, int32_t rank, int32_t world, int32_t H, int32_t top_k,
+                  int32_t send_cap, int32_t recv_cap, void* recv_buf, int32_t* info, gemms_stream_t stream);
+
+/* gemms_ep_expert_ffn over the first info[0] of R_cap received rows (the row
+ * count is read on the device; launches are sized for R_cap). */
+int gemms_ep_expert_ffn_dev(const void* recv_buf, int32_t R_cap, const int32_t* info, int32_t P_max, int32_t H,
+                            int32_t I, int32_t top_k, int32_t E_local, int32_t local_expert_offset,
+                            int32_t inter_planes, const void* w13, const float* w13_scale, const void* w2,
+                            const float* w2_scale, float* out_rows, void* workspace, size_t ws_bytes,
+                            gemms_stream_t stream);
+
+/* gemms_ep_pack_back over the first info[0] of R_cap rows. */
+int gemms_ep_pack_back_dev(const float* rows, int32_t R_cap, const int32_t* info, int32_t H, void* packed,
+                           gemms_stream_t stream);
+
+/* gemms_ep_combine_rows with the row offsets taken from gemms_ep_pull's info
+ * (info[88 + d]) on the device; every rank's packed combine rows hold
+ * recv_cap rows, and a row index outside [0, recv_cap) (only after a pull
+ * that raised a flag) is skipped, not read. */
+int gemms_ep_combine_peer(const float* acc, const void* const* row_base, const int32_t* info,
+                          const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, int32_t recv_cap,
+                          void* out_bf16, gemms_stream_t stream);
+
+/* CTAs of gemms_ep_pull's row copy for later calls (0 = two per SM, the
+ * default); returns the previous value, or GEMMS_ERR_ARG if negative. */
+int gemms_ep_set_pull_ctas(int32_t ctas);
+
 /* Bounds the grid of the persistent grouped-GEMM kernels to max_ctas CTAs
  * (0 = one per SM, the default) for launches made after the call, from any
  * thread.  Returns the previous bound, or GEMMS_ERR_ARG for a negative value.

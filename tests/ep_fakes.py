@@ -2,9 +2,10 @@
 
 They follow the contracts of ``include/gemms_moe.h`` (packed row layout,
 destination grouping in token order, fp32 pre-reduced rows, deterministic
-combine) with the oracle's fp32 arithmetic, so that ``gemms_b200.ep.moe_ep``'s
-host logic -- count exchange, split sizes, the two all-to-alls and the
-combine mapping -- runs on gloo ranks without a GPU.
+combine, the device-driven exchange's region layout and plan) with the
+oracle's fp32 arithmetic, so that ``gemms_b200.ep.moe_ep``'s host logic --
+count exchange, split sizes, the two all-to-alls, the exchange regions and
+barriers, the combine mapping -- runs on gloo ranks without a GPU.
 """
 from __future__ import annotations
 
@@ -33,7 +34,7 @@ class CpuEpKernels:
         idx, dense, _, _ = R.route(logits, bias, n_group, topk_group, top_k, rsf)
         return idx.to(torch.int32), torch.gather(dense, 1, idx)
 
-    def dispatch(self, idx, w, x, world, E_local):
+    def dispatch(self, idx, w, x, world, E_local, region=None):
         T, H = x.shape
         k = idx.shape[1]
         rb = EP.row_bytes(H, k)
@@ -59,6 +60,11 @@ class CpuEpKernels:
             ws = torch.where(here, w[t], torch.zeros_like(w[t])).to(torch.float32)
             buf[r, H + 4 * KB:H + 4 * KB + 4 * k] = ids.view(torch.uint8)
             buf[r, H + 4 * KB + 4 * k:H + 4 * KB + 8 * k] = ws.view(torch.uint8)
+        if region is not None:  # the exchange region's header and send rows
+            region.hdr.copy_(counts)
+            region.send.zero_()
+            region.send[:len(rows)] = buf[:len(rows)]
+            buf = region.send
         return counts, send_row_of, buf, xq, xq_scale
 
     def expert_ffn(self, recv_buf, Rn, P, H, I, top_k, E_local, offset, planes, w13, w13_scale, w2, w2_scale):
@@ -107,30 +113,82 @@ class CpuEpKernels:
             packed[r, 2 * H:2 * H + 4] = torch.tensor([math.ldexp(1.0, e)], dtype=torch.float32).view(torch.uint8)
         return packed
 
-    # peer combine: each rank's buffer stands for its symmetric allocation; the
-    # "barrier" hands every rank a copy of all buffers (gloo all_gather), and
-    # the combine reads rows from them with the offsets moe_ep computed.
-    def peer_buffers(self, group, cap_rows, H):
-        local = torch.zeros(max(cap_rows, 1) * EP.back_row_bytes(H), dtype=torch.uint8)
-        return local, None
-
-    def peer_publish(self, group, local, peers):
+    # device-driven exchange: each rank's region is a set of CPU tensors; the
+    # barrier hands every rank copies of all regions (gloo all_gather), which
+    # stand for the peer mappings the pull and the combine read.
+    def exchange_region(self, group, send_cap, recv_cap, H, top_k):
         import torch.distributed as dist
-        bufs = [torch.empty_like(local) for _ in range(dist.get_world_size(group))]
-        dist.all_gather(bufs, local, group=group)
-        return bufs
 
-    def combine_rows(self, acc, peers, row_add, send_row_of, world):
+        class Region:
+            pass
+        world = dist.get_world_size(group)
+        reg = Region()
+        reg.world, reg.send_cap, reg.recv_cap = world, send_cap, recv_cap
+        reg.rb, reg.rbb = EP.row_bytes(H, top_k), EP.back_row_bytes(H)
+        reg.hdr = torch.zeros((2, world), dtype=torch.int32)
+        reg.send = torch.zeros((send_cap, reg.rb), dtype=torch.uint8)
+        reg.back = torch.zeros(recv_cap * reg.rbb, dtype=torch.uint8)
+        return reg
+
+    def peer_barrier(self, group, reg):
+        import torch.distributed as dist
+        world = dist.get_world_size(group)
+        reg.peer_hdr = [torch.empty_like(reg.hdr) for _ in range(world)]
+        reg.peer_send = [torch.empty_like(reg.send) for _ in range(world)]
+        reg.peer_back = [torch.empty_like(reg.back) for _ in range(world)]
+        dist.all_gather(reg.peer_hdr, reg.hdr, group=group)
+        dist.all_gather(reg.peer_send, reg.send, group=group)
+        dist.all_gather(reg.peer_back, reg.back, group=group)
+
+    def pull(self, reg, rank, world, H, top_k):
+        """The plan of gemms_ep_pull (info layout of include/gemms_moe.h) and the copy."""
+        m = [reg.peer_hdr[s][0].tolist() for s in range(world)]
+        mp = [reg.peer_hdr[s][1].tolist() for s in range(world)]
+        to_me = [m[s][rank] for s in range(world)]
+        total = sum(to_me)
+        flags = 1 if total > reg.recv_cap else 0
+        if any(sum(m[s]) > reg.send_cap or min(m[s]) < 0 for s in range(world)):
+            flags |= 2
+        info = torch.zeros(128, dtype=torch.int32)
+        R = 0 if flags else total
+        info[0], info[1], info[2] = R, (0 if flags else sum(mp[s][rank] for s in range(world))), flags
+        start = 0
+        recv = torch.zeros((reg.recv_cap, reg.rb), dtype=torch.uint8)
+        for s in range(world):
+            info[8 + s] = start
+            info[48 + s] = sum(m[s][:rank])
+            info[88 + s] = sum(m[q][s] for q in range(rank)) - sum(m[rank][:s])
+            if not flags:
+                o = int(info[48 + s])
+                recv[start:start + to_me[s]] = reg.peer_send[s][o:o + to_me[s]]
+            start += to_me[s]
+        info[8 + world] = total
+        return recv, info
+
+    def expert_ffn_dev(self, recv_buf, info, R_cap, P_cap, H, I, top_k, E_local, offset, planes, w13, w13_scale,
+                       w2, w2_scale):
+        Rn = int(info[0])
+        out = torch.zeros((R_cap, H), dtype=torch.float32)
+        out[:Rn] = self.expert_ffn(recv_buf[:Rn], Rn, int(info[1]), H, I, top_k, E_local, offset, planes, w13,
+                                   w13_scale, w2, w2_scale)
+        return out
+
+    def pack_back_dev(self, rows, info, reg):
+        self.pack_back(rows[:int(info[0])], out=reg.back)
+
+    def combine_peer(self, acc, reg, info, send_row_of, world):
         out = acc.clone()
         H = acc.shape[1]
-        rbb = EP.back_row_bytes(H)
         for t in range(acc.shape[0]):
             for d in range(world):
                 r = int(send_row_of[t, d])
                 if r >= 0:
-                    row = peers[d].view(-1, rbb)[r + row_add[d]]
+                    row = reg.peer_back[d].view(-1, reg.rbb)[r + int(info[88 + d])]
                     out[t] += self.unpack_back(row, H)
         return out.to(torch.bfloat16)
+
+    def exchange_flags(self, reg):
+        return 0
 
     @staticmethod
     def unpack_back(packed_row, H):

@@ -125,6 +125,25 @@ def test_new_entry_points_validate_arguments_without_gpu():
     assert L.gemms_set_gemm_ctas(-1) == ERR_ARG
     prev = L.gemms_set_gemm_ctas(7)
     assert L.gemms_set_gemm_ctas(prev) == 7
+    # device-driven exchange: region size = 256-byte count header + send rows
+    rb = L.gemms_ep_row_bytes(7168, 8)
+    assert L.gemms_ep_region_bytes(100, 7168, 8) == 256 + 100 * rb
+    assert L.gemms_ep_region_bytes(-1, 7168, 8) == 0 and L.gemms_ep_region_bytes(1, 7100, 8) == 0
+    info = ctypes.c_void_p(64)  # never dereferenced: every call below fails its host checks
+    assert L.gemms_ep_pull(bases, 0, 2, 7168, 8, 10, 10, None, info, None) == ERR_ARG    # NULL region addresses
+    assert L.gemms_ep_pull(bases, 2, 2, 7168, 8, 10, 10, None, info, None) == ERR_SHAPE  # rank >= world
+    assert L.gemms_ep_pull(bases, 0, 33, 7168, 8, 10, 10, None, info, None) == ERR_SHAPE
+    assert L.gemms_ep_pull(None, 0, 2, 7168, 8, 10, 10, None, None, None) == ERR_ARG
+    assert L.gemms_ep_pack_back_dev(None, 4, None, 7168, None, None) == ERR_ARG
+    assert L.gemms_ep_pack_back_dev(None, 0, None, 7168, None, None) == 0
+    assert L.gemms_ep_combine_peer(None, bases, None, None, 4, 7168, 2, 8, None, None) == ERR_ARG
+    assert L.gemms_ep_combine_peer(None, bases, info, None, 4, 7168, 33, 8, None, None) == ERR_SHAPE
+    assert L.gemms_ep_combine_peer(None, bases, info, None, 4, 7168, 2, 0, None, None) == ERR_SHAPE
+    assert L.gemms_ep_expert_ffn_dev(None, 4, None, 32, 7168, 2048, 8, 32, 0, 2, None, None, None, None, None,
+                                     None, 0, None) == ERR_ARG
+    assert L.gemms_ep_set_pull_ctas(-1) == ERR_ARG
+    prev = L.gemms_ep_set_pull_ctas(16)
+    assert L.gemms_ep_set_pull_ctas(prev) == 16
 
 
 def test_stall_hook_rejects_bad_arguments():

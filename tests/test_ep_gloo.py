@@ -2,7 +2,8 @@
 
 The device side is replaced by CPU stand-ins (tests/ep_fakes.py) that follow
 the C ABI's contracts with the oracle's arithmetic; the exchange itself (count
-all-to-all, split sizes, dispatch and combine all-to-alls, combine mapping) is
+all-to-all, split sizes, dispatch and combine all-to-alls, or the
+device-driven exchange's regions, barriers and plan; the combine mapping) is
 the product code.  The 2-rank result must equal the single-process oracle over
 all tokens.  A second test makes one rank leave before the first collective:
 the remaining rank must raise within its process-group timeout, not hang.
@@ -37,7 +38,7 @@ def _inputs():
     return W.make_inputs(SHAPE, seed=4)
 
 
-def _ep_worker(rank, world, port, outdir, combine="nccl"):
+def _ep_worker(rank, world, port, outdir, exchange="nccl"):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from tests.ep_fakes import CpuEpKernels
@@ -55,18 +56,20 @@ def _ep_worker(rank, world, port, outdir, combine="nccl"):
                     d["w2_scale"][el], shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"],
                     shared_w2=d["shared_w2"], shared_w2_scale=d["shared_w2_scale"], n_group=SHAPE.n_group,
                     topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, routed_scaling_factor=SHAPE.rsf,
-                    group=dist.group.WORLD, kernels=K, combine=combine)
+                    group=dist.group.WORLD, kernels=K, exchange=exchange)
     torch.save(out, os.path.join(outdir, f"out{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("combine,world", [("nccl", 2), ("peer", 2), ("nccl", 4), ("peer", 4)])
-def test_ep_ranks_match_single_process_oracle(combine, world):
-    """Both combine modes: the all-to-all, and the peer read of rows left on
-    the rank that computed them (row offsets from the count matrix)."""
+@pytest.mark.parametrize("exchange,world", [("nccl", 2), ("peer", 2), ("nccl", 4), ("peer", 4)])
+def test_ep_ranks_match_single_process_oracle(exchange, world):
+    """Both exchange modes: the all-to-alls with host split sizes, and the
+    device-driven exchange (rows pulled from the senders' regions, result
+    rows read from the computing rank's region, offsets planned from the
+    counts in the region headers)."""
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_ep_worker, args=(world, _free_port(), tmp, combine), nprocs=world, join=True)
+        mp.spawn(_ep_worker, args=(world, _free_port(), tmp, exchange), nprocs=world, join=True)
         got = torch.cat([torch.load(os.path.join(tmp, f"out{r}.pt")) for r in range(world)])
     d = _inputs()
     ref = R.moe_layer(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
@@ -101,7 +104,7 @@ def test_pack_back_round_trip():
         assert err <= 2 ** -11, (r, err)
 
 
-def _leaver_worker(rank, world, port, outdir, combine="nccl", leave="before_layer"):
+def _leaver_worker(rank, world, port, outdir, exchange="nccl", leave="before_layer"):
     import sys
     import time
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -122,6 +125,11 @@ def _leaver_worker(rank, world, port, outdir, combine="nccl", leave="before_laye
                 os._exit(0)
             return super().pack_back(rows, out)
 
+        def pack_back_dev(self, rows, info, reg):
+            if rank == 1:
+                os._exit(0)
+            return super().pack_back_dev(rows, info, reg)
+
     K = (Leaving if leave == "before_combine" else CpuEpKernels)(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
     sl, el = slice(rank * T, (rank + 1) * T), slice(rank * El, (rank + 1) * El)
     t0 = time.time()
@@ -129,7 +137,7 @@ def _leaver_worker(rank, world, port, outdir, combine="nccl", leave="before_laye
     try:
         EP.moe_ep(d["x"][sl], d["router_w"], d["router_bias"], d["w13"][el], d["w13_scale"][el], d["w2"][el],
                   d["w2_scale"][el], n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k,
-                  routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K, combine=combine)
+                  routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K, exchange=exchange)
     except RuntimeError as e:  # gloo: timeout or connection closed by the departed peer
         status = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
     if rank == 0:
@@ -137,16 +145,16 @@ def _leaver_worker(rank, world, port, outdir, combine="nccl", leave="before_laye
             f.write(status)
 
 
-@pytest.mark.parametrize("combine,leave", [("nccl", "before_layer"), ("nccl", "before_combine"),
-                                           ("peer", "before_combine")])
-def test_ep_rank_that_leaves_is_detected(combine, leave):
+@pytest.mark.parametrize("exchange,leave", [("nccl", "before_layer"), ("nccl", "before_combine"),
+                                            ("peer", "before_layer"), ("peer", "before_combine")])
+def test_ep_rank_that_leaves_is_detected(exchange, leave):
     """A rank that is gone (before the layer, or after the dispatch and before
     its rows go back) makes the other rank's next collective (the count
-    exchange, the combine all-to-all, or the peer mode's barrier) fail within
+    exchange, the combine all-to-all, or the peer mode's barriers) fail within
     the process group's timeout instead of waiting for ever."""
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_leaver_worker, args=(world, _free_port(), tmp, combine, leave), nprocs=world, join=True)
+        mp.spawn(_leaver_worker, args=(world, _free_port(), tmp, exchange, leave), nprocs=world, join=True)
         status = open(os.path.join(tmp, "status.txt")).read()
     assert status.startswith("error after"), status
     secs = float(status.split()[2].rstrip("s:"))

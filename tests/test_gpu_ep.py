@@ -28,9 +28,9 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, outdir, case, combine="nccl"):
+def _worker(rank, world, port, outdir, case, exchange="nccl"):
     import sys
-    os.environ["GEMMS_EP_COMBINE"] = combine
+    os.environ["GEMMS_EP_EXCHANGE"] = exchange
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import gemms_b200
 
@@ -54,10 +54,10 @@ def _worker(rank, world, port, outdir, case, combine="nccl"):
     torch.cuda.synchronize()
     torch.save(out.cpu(), os.path.join(outdir, f"ep{rank}.pt"))
     # A run of calls with different token counts and inputs (so different
-    # routing): the peer combine alternates between two symmetric buffers and
-    # a rank rewrites buffer i % 2 while relying on call i - 1's barrier for
-    # the peers' reads of call i - 2; the last call needs more rows than any
-    # before it and grows the buffers.  Each call is checked against the
+    # routing): with the device-driven exchange a rank rewrites its one
+    # exchange region every call, relying on the previous call's barriers for
+    # the peers' reads; the last call needs more rows than any before it and
+    # grows the regions (collectively).  Each call is checked against the
     # single-GPU layer on the same tokens.
     seq = []
     for i, tpr in enumerate((T, T // 2, T // 4, T // 2, T, 2 * T)):
@@ -67,6 +67,10 @@ def _worker(rank, world, port, outdir, case, combine="nccl"):
                            ep_group=dist.group.WORLD, **kw)
         seq.append((x_all, o))
     torch.cuda.synchronize()
+    if exchange == "peer":  # no capacity or count flag raised by any pull
+        from gemms_b200 import ep as EPm
+        K = EPm._cuda_kernels()
+        assert K._symm and all(K.exchange_flags(r) == 0 for r in K._symm.values())
     torch.save([o.cpu() for _, o in seq], os.path.join(outdir, f"seq{rank}.pt"))
     if rank == 0:
         single, idx, w, counts, logits = gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"],
@@ -82,31 +86,32 @@ def _worker(rank, world, port, outdir, case, combine="nccl"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("case,combine", [("c0", "nccl"), ("v3", "nccl"), ("c0", "peer"), ("v3", "peer")])
-def test_ep2_matches_single_gpu_and_oracle(case, combine):
-    """Both combine modes; "peer" reads the result rows from the other GPU's
-    symmetric buffer over NVLink."""
+@pytest.mark.parametrize("case,exchange", [("c0", "nccl"), ("v3", "nccl"), ("c0", "peer"), ("v3", "peer")])
+def test_ep2_matches_single_gpu_and_oracle(case, exchange):
+    """Both exchange modes; "peer" pulls the dispatched rows from, and reads
+    the result rows in, the other GPU's exchange region over NVLink, with no
+    host read of the counts."""
     from oracle import reference_moe as R
     from tests import helpers as Hh
 
     world = 2
     sh = CASES[case]
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_worker, args=(world, _free_port(), tmp, case, combine), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), tmp, case, exchange), nprocs=world, join=True)
         ep = torch.cat([torch.load(os.path.join(tmp, f"ep{r}.pt")) for r in range(world)])
         seqs = [torch.load(os.path.join(tmp, f"seq{r}.pt")) for r in range(world)]
         s = torch.load(os.path.join(tmp, "single.pt"))
     for i, want in enumerate(s["seq"]):
         got = torch.cat([seqs[r][i] for r in range(world)])
         mi = R.compare(got, want)
-        print(f"EP2 {case} {combine} call {i} ({got.shape[0]} tokens) vs single GPU", mi)
+        print(f"EP2 {case} {exchange} call {i} ({got.shape[0]} tokens) vs single GPU", mi)
         assert mi["mae_rms"] < 3e-4 and mi["max_rel"] < 1e-2, f"call {i}: {mi}"
     m = R.compare(ep, s["single"])
     # The combine rows travel as fp16 with an exact power-of-two scale (2^-11
     # relative), which flips a few bf16 output roundings against the single-GPU
     # layer (~1e-4 of RMS); a misrouted row would cost errors of the output's size.
     assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, f"EP vs single GPU: {m}"
-    print(f"EP2 {case} {combine} vs single GPU", m)
+    print(f"EP2 {case} {exchange} vs single GPU", m)
     # oracle on a row sample (CPU weights regenerated from the same seed on GPU 0)
     d = W.make_inputs(sh, seed=5, device="cuda:0")
     rows = [0, 1, sh.T // 2, sh.T - 1]
