@@ -59,7 +59,7 @@ class GemmsMoeShape(ctypes.Structure):
         ("T", c_int32), ("H", c_int32), ("I", c_int32), ("E", c_int32), ("E_local", c_int32),
         ("local_expert_offset", c_int32), ("n_group", c_int32), ("topk_group", c_int32), ("top_k", c_int32),
         ("has_shared", c_int32), ("input_mode", c_int32), ("bias_bf16", c_int32), ("inter_planes", c_int32),
-        ("routed_scaling_factor", c_float),
+        ("routed_scaling_factor", c_float), ("deterministic", c_int32),
     ]
 
 

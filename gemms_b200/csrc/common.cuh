@@ -142,9 +142,17 @@ struct Gemm2Args {
   int H, I, planes;
   const int32_t* row_dest; const float* row_weight;                        // [R]
   float* out;                                                               // [n_dest, H] fp32 (+=)
+  float* pair_out;  // when set: weighted row r stored to pair_out[r] ([R, H] fp32), out unused
   int* err;
 };
 int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
+
+// Deterministic combine: out[t] = round(residual[t] + sum over j < K of
+// pair_out[pair_row[t, j]] (rows < 0 skipped) + pair_out[*shared_row0 + t]),
+// added in that order in fp32; bf16 out (residual optional) or fp32 out.
+int launch_combine_slots(const float* pair_out, const int32_t* pair_row, int T, int K, int H,
+                         const int32_t* shared_row0, const __nv_bfloat16* residual, __nv_bfloat16* out_bf16,
+                         float* out_f32, const int32_t* T_dev, cudaStream_t s);
 
 // Router GEMM (router_gemm.cu): logits = x . router_w^T via a bf16 hi/lo split.
 struct RouterPlan {

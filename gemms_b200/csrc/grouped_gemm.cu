@@ -101,6 +101,7 @@ struct GemmParams {
   const int32_t* row_dest;
   const float* row_weight;
   float* out;
+  float* pair_out;  // deterministic combine: weighted rows stored per grouped row, no atomics
   int H;
   int* err;
   // Bounded waits: cycles before a pipeline wait gives up (product default
@@ -470,12 +471,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // shared memory and comes back with 4 lanes per row, so every vector
         // RED covers 64 contiguous bytes of 8 rows.
         float* stage = reinterpret_cast<float*>(smem + C::kRingBytes + 4096) + ew * (32 * 20);
-        const int dst_me = valid ? p.row_dest[row0 + r] : -1;
+        // With pair_out the row goes to its own grouped row instead (a plain
+        // store; the per-token sum happens later in a fixed order).
+        const bool slots = p.pair_out != nullptr;
+        const int dst_me = valid ? (slots ? row0 + r : p.row_dest[row0 + r]) : -1;
         const float wgt = valid ? p.row_weight[row0 + r] : 0.f;
         int dst_i[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst_i[i] = __shfl_sync(0xffffffffu, dst_me, 8 * i + (lane >> 2));
-        float* obase = p.out + (size_t)nt * BN + 128 * h + 4 * (lane & 3);
+        float* obase = (slots ? p.pair_out : p.out) + (size_t)nt * BN + 128 * h + 4 * (lane & 3);
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
 #pragma unroll
@@ -489,7 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = 8 * i + (lane >> 2);
             if (dst_i[i] >= 0) {
               const float4 v = *reinterpret_cast<const float4*>(stage + row * 20 + 4 * (lane & 3));
-              atomicAdd(reinterpret_cast<float4*>(obase + (size_t)dst_i[i] * p.H + 16 * ch), v);
+              float4* o = reinterpret_cast<float4*>(obase + (size_t)dst_i[i] * p.H + 16 * ch);
+              if (slots)
+                *o = v;
+              else
+                atomicAdd(o, v);
             }
           }
           __syncwarp();
@@ -659,6 +667,7 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.row_dest = a.row_dest;
   p.row_weight = a.row_weight;
   p.out = a.out;
+  p.pair_out = a.pair_out;
   p.H = a.H;
   p.I = a.I;
   p.err = a.err;

@@ -16,7 +16,8 @@ struct FwdLayout {
   int T, K, H, I, E_loc, shared, planes;
   int R_max, groups, max_tiles, scale_ld;
   size_t err, counts, topk_idx, topk_w, pair_row, offsets, tile_group, tile_row0, tile_rows, num_tiles;
-  size_t row_token, row_weight, a_rows, a_scale, inter, inter_scale, out_acc, total;
+  size_t row_token, row_weight, a_rows, a_scale, inter, inter_scale, out_acc, pair_out, total;
+  int det;  // deterministic combine: per-row results in pair_out, summed per token in slot order
   RouterPlan router;
   size_t router_planes, router_partials;  // router GEMM scratch (GEMMS_INPUT_BF16 only)
   size_t head_bytes;  // [0, head_bytes) is zeroed each call (error word + counts)
@@ -58,7 +59,11 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.a_scale = take(sizeof(float) * (size_t)(L.H / kBlock) * L.scale_ld);
   L.inter = take((size_t)std::max(L.R_max, 1) * L.planes * L.I);
   L.inter_scale = take(sizeof(float) * (size_t)(L.I / kBlock) * L.scale_ld);
-  L.out_acc = take(sizeof(float) * (size_t)L.T * L.H);
+  L.det = s.deterministic ? 1 : 0;
+  if (L.det)
+    L.pair_out = take(sizeof(float) * (size_t)std::max(L.R_max, 1) * L.H);
+  else
+    L.out_acc = take(sizeof(float) * (size_t)L.T * L.H);
   if (s.input_mode == GEMMS_INPUT_BF16) {
     L.router = router_plan(s.T, s.H, s.E);
     L.router_planes = L.router.split_bytes ? take(L.router.split_bytes) : 0;
@@ -158,7 +163,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   void* ws = workspace;
   int* err = at<int>(ws, L.err);
   GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, L.head_bytes, st));
-  GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
+  if (!L.det) GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
 
   RouteArgs ra{};
   if (gemm_router) {
@@ -290,15 +295,22 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   g2.planes = L.planes;
   g2.row_dest = sa.row_token;
   g2.row_weight = sa.row_weight;
-  g2.out = at<float>(ws, L.out_acc);
+  g2.out = L.det ? nullptr : at<float>(ws, L.out_acc);
+  g2.pair_out = L.det ? at<float>(ws, L.pair_out) : nullptr;
   g2.err = err;
   if (!g2.w2) g2.w2 = g2.sw2;
   if ((rc = launch_gemm2(g2, st))) return rc;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[2], st));
 
-  if ((rc = launch_to_bf16(g2.out, static_cast<__nv_bfloat16*>(args->out), (size_t)s.T * s.H,
-                           static_cast<const __nv_bfloat16*>(args->residual), st)))
+  if (L.det) {
+    if ((rc = launch_combine_slots(g2.pair_out, ra.pair_row, s.T, s.top_k, s.H, qa.shared_row0,
+                                   static_cast<const __nv_bfloat16*>(args->residual),
+                                   static_cast<__nv_bfloat16*>(args->out), nullptr, nullptr, st)))
+      return rc;
+  } else if ((rc = launch_to_bf16(g2.out, static_cast<__nv_bfloat16*>(args->out), (size_t)s.T * s.H,
+                                  static_cast<const __nv_bfloat16*>(args->residual), st))) {
     return rc;
+  }
 
   if (args->topk_idx_out)
     GEMMS_CUDA_TRY(cudaMemcpyAsync(args->topk_idx_out, ra.topk_idx, sizeof(int32_t) * (size_t)s.T * s.top_k,

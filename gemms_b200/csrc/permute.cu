@@ -144,6 +144,65 @@ __global__ void to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict_
   }
 }
 
+// Block per token: the token's slot rows (its top-k grouped rows in slot
+// order, then the shared expert's) are summed in that fixed order, so the
+// result does not depend on which CTA finished first.
+__global__ void __launch_bounds__(256, 4) combine_slots_kernel(const float* __restrict__ pair_out,
+                                                               const int32_t* __restrict__ pair_row, int T, int K,
+                                                               int H, const int32_t* __restrict__ shared_row0,
+                                                               const uint2* __restrict__ residual,
+                                                               uint2* __restrict__ out_bf16,
+                                                               float4* __restrict__ out_f32,
+                                                               const int32_t* __restrict__ T_dev) {
+  __shared__ int s_rows[17];
+  __shared__ int s_n;
+  const int t = blockIdx.x;
+  if (T_dev && t >= *T_dev) return;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    const int r = lane < K ? pair_row[(size_t)t * K + lane] : -1;
+    const unsigned b = __ballot_sync(0xffffffffu, r >= 0);
+    if (r >= 0) s_rows[__popc(b & ((1u << lane) - 1u))] = r;
+    if (lane == 0) {
+      int n = __popc(b);
+      if (shared_row0) s_rows[n++] = *shared_row0 + t;
+      s_n = n;
+    }
+  }
+  __syncthreads();
+  const int n = s_n;
+  const int H4 = H / 4;
+  for (int c = threadIdx.x; c < H4; c += blockDim.x) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < n; ++i) {
+      const float4 x = reinterpret_cast<const float4*>(pair_out + (size_t)s_rows[i] * H)[c];
+      v.x += x.x;
+      v.y += x.y;
+      v.z += x.z;
+      v.w += x.w;
+    }
+    const size_t o = (size_t)t * H4 + c;
+    if (out_f32) {
+      out_f32[o] = v;
+      continue;
+    }
+    if (residual) {
+      const uint2 rr = residual[o];
+      const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.x));
+      const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.y));
+      v.x += r0.x;
+      v.y += r0.y;
+      v.z += r1.x;
+      v.w += r1.y;
+    }
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&a);
+    w.y = *reinterpret_cast<uint32_t*>(&b);
+    out_bf16[o] = w;
+  }
+}
 }  // namespace
 
 int launch_permute(const PermuteArgs& a, cudaStream_t s) {
@@ -173,6 +232,21 @@ int launch_to_bf16(const float* in, __nv_bfloat16* out, size_t n, const __nv_bfl
   const int blocks = static_cast<int>(std::min<size_t>((n4 + 255) / 256, (size_t)num_sms() * 8));
   to_bf16_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(in), reinterpret_cast<uint2*>(out), n4,
                                         reinterpret_cast<const uint2*>(residual));
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int launch_combine_slots(const float* pair_out, const int32_t* pair_row, int T, int K, int H,
+                         const int32_t* shared_row0, const __nv_bfloat16* residual, __nv_bfloat16* out_bf16,
+                         float* out_f32, const int32_t* T_dev, cudaStream_t s) {
+  if (T <= 0) return GEMMS_OK;
+  if (H % 4 || K < 1 || K > 16 || (!out_bf16 && !out_f32)) return GEMMS_ERR_SHAPE;
+  if ((residual && (reinterpret_cast<uintptr_t>(residual) & 7u)) || !aligned16(pair_out) ||
+      (out_f32 && !aligned16(out_f32)) || (out_bf16 && (reinterpret_cast<uintptr_t>(out_bf16) & 7u)))
+    return GEMMS_ERR_ALIGN;
+  combine_slots_kernel<<<T, 256, 0, s>>>(pair_out, pair_row, T, K, H, shared_row0,
+                                         reinterpret_cast<const uint2*>(residual), reinterpret_cast<uint2*>(out_bf16),
+                                         reinterpret_cast<float4*>(out_f32), T_dev);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

@@ -122,11 +122,14 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         hidden_states_scale: torch.Tensor, gemm1_weights: torch.Tensor, gemm1_weights_scale: torch.Tensor,
         gemm2_weights: torch.Tensor, gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
         routed_scaling_factor: float, *, n_group: int = 8, topk_group: int = 4, top_k: int = 8,
-        inter_planes: int = 2, return_routing: bool = False):
+        inter_planes: int = 2, return_routing: bool = False, deterministic: bool = False):
     """Drop-in for ``flashinfer_baseline.run`` (``:5-16``) on B200.
 
     The reference fixes n_group=8, topk_group=4, top_k=8 (``:48-50``); they are
-    keyword parameters here with those defaults.
+    keyword parameters here with those defaults.  ``deterministic=True`` makes
+    the combine bit-reproducible (per-token sum of the expert rows in slot
+    order instead of fp32 atomics; the reference's ``index_add_`` order,
+    ``:166-169``, is also fixed).
     """
     dev = _check_cuda(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
@@ -155,7 +158,8 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     shape = GemmsMoeShape(T=T, H=H, I=I, E=E, E_local=E_local, local_expert_offset=int(local_expert_offset),
                           n_group=n_group, topk_group=topk_group, top_k=top_k, has_shared=0,
                           input_mode=_lib.GEMMS_INPUT_FP8, bias_bf16=int(routing_bias.dtype == torch.bfloat16),
-                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor))
+                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor),
+                          deterministic=int(deterministic))
     args = GemmsMoeArgs()
     args.routing_logits = _ptr(routing_logits)
     args.routing_bias = _ptr(routing_bias)
@@ -212,7 +216,7 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
         n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
         inter_planes: int = 2, logits: torch.Tensor | None = None, ep_group=None,
         return_routing: bool = False, profile_events=None, residual: torch.Tensor | None = None,
-        ep_exchange: str | None = None, max_tokens_per_rank: int | None = None):
+        ep_exchange: str | None = None, max_tokens_per_rank: int | None = None, deterministic: bool = False):
     """DeepSeek-V3 MoE layer forward: bf16 x [T, H] -> bf16 [T, H].
 
     ``w13`` [E, 2I, H] / ``w2`` [E, H, I] are e4m3 with fp32 128x128 block
@@ -226,10 +230,17 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
     ``torch.cuda.Event``) brackets GEMM1 and GEMM2 for kernel timing.
     ``residual`` (bf16 [T, H]) is added to the layer's fp32 result before the
     single rounding to bf16 (the decoder's residual add, fused).
+    ``deterministic=True`` (single GPU) makes the result bit-reproducible run
+    to run: each (token, expert) row is stored and the rows are summed per
+    token in slot order (k routed experts, then the shared expert) instead of
+    added with fp32 atomics, at the cost of writing and reading them once
+    (R x H x 4 bytes of workspace, R = T*top_k (+T)).
     """
     if ep_group is not None:
         if residual is not None:
             raise ShapeError("residual is not supported with ep_group")
+        if deterministic:
+            raise ShapeError("deterministic is not supported with ep_group")
         from . import ep
         return ep.moe_ep(x, router_w, router_bias, w13, w13_scale, w2, w2_scale, shared_w13=shared_w13,
                          shared_w13_scale=shared_w13_scale, shared_w2=shared_w2, shared_w2_scale=shared_w2_scale,
@@ -263,7 +274,8 @@ def moe(x: torch.Tensor, router_w: torch.Tensor, router_bias: torch.Tensor, w13:
     shape = GemmsMoeShape(T=T, H=H, I=I, E=E, E_local=E, local_expert_offset=0, n_group=n_group,
                           topk_group=topk_group, top_k=top_k, has_shared=int(has_shared),
                           input_mode=_lib.GEMMS_INPUT_BF16, bias_bf16=int(bias.dtype == torch.bfloat16),
-                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor))
+                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor),
+                          deterministic=int(deterministic))
     args = GemmsMoeArgs()
     args.routing_logits = _ptr(logits)  # None: the router GEMM runs inside gemms_moe_fwd
     args.router_w = _ptr(router_w)
@@ -345,7 +357,7 @@ def moe_block(h: torch.Tensor, norm_weight: torch.Tensor, router_w: torch.Tensor
               eps: float = 1e-6, shared_w13: torch.Tensor | None = None, shared_w13_scale: torch.Tensor | None = None,
               shared_w2: torch.Tensor | None = None, shared_w2_scale: torch.Tensor | None = None,
               n_group: int = 8, topk_group: int = 4, top_k: int = 8, routed_scaling_factor: float = 2.5,
-              inter_planes: int = 2) -> torch.Tensor:
+              inter_planes: int = 2, deterministic: bool = False) -> torch.Tensor:
     """The MoE half of a DeepSeek-V3 decoder layer on the residual stream h
     (bf16 [T, H]): h + moe(rmsnorm(h)).  RMSNorm and the 1x128 quantisation
     run as one kernel whose e4m3 rows feed the experts directly (no second
@@ -366,7 +378,8 @@ def moe_block(h: torch.Tensor, norm_weight: torch.Tensor, router_w: torch.Tensor
     shape = GemmsMoeShape(T=T, H=H, I=I, E=E, E_local=E, local_expert_offset=0, n_group=n_group,
                           topk_group=topk_group, top_k=top_k, has_shared=int(has_shared),
                           input_mode=_lib.GEMMS_INPUT_FP8, bias_bf16=int(router_bias.dtype == torch.bfloat16),
-                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor))
+                          inter_planes=inter_planes, routed_scaling_factor=float(routed_scaling_factor),
+                          deterministic=int(deterministic))
     args = GemmsMoeArgs()
     args.routing_logits = _ptr(logits)
     args.routing_bias = _ptr(router_bias)

@@ -71,6 +71,11 @@ typedef struct {
   int32_t bias_bf16;            /* 1: routing_bias is bf16, 0: fp32                */
   int32_t inter_planes;         /* e4m3 planes of the SwiGLU intermediate: 2 or 3  */
   float routed_scaling_factor;
+  int32_t deterministic;        /* 1: bit-reproducible combine -- each (token,     */
+                                /* expert) result row is stored, then summed per   */
+                                /* token in slot order (k routed, then shared);    */
+                                /* 0: fp32 vector atomics (faster, order-dependent */
+                                /* in the last bits); 1 adds R*H*4 workspace bytes */
 } GemmsMoeShape;
 
 typedef struct {
