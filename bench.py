@@ -559,9 +559,26 @@ def gpu_arm(a):
                "path": "pinned host x -> gemms_b200.MoePipeline (public API; copies overlapped with the "
                        "layer on side streams) -> pinned host out, every step, every rank"}
     decode = None
+    det = None
     if group is None and cfg == "c1":
         hbm_peak = _peaks()[0]
         decode = decode_sweep(d, {k: v for k, v in kw.items() if k != "ep_group"}, sh, hbm_peak)
+        # the same step with the deterministic (fixed-order) combine
+        kw1 = {k: v for k, v in kw.items() if k != "ep_group"}
+        for _ in range(2):
+            gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+                           deterministic=True, **kw1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+                           deterministic=True, **kw1)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_det = e0.elapsed_time(e1) / a.steps
+        det = {"what": "same c1 step with deterministic=True (per-token fixed-order combine, bit-reproducible)",
+               "ms_per_step": round(ms_det, 4), "tokens_per_s": round(base.T / (ms_det / 1e3), 1)}
     clocks = sampler.stop() if sampler else None
 
     tokens_total = base.T
@@ -588,6 +605,9 @@ def gpu_arm(a):
                                    "best of 10 on rank 0's GPU, times the GPU count"},
             "gpu_launches": (launches_per_step * a.steps) if launches_per_step is not None else None,
             "e2e": e2e, "clocks": clocks}
+    if det is not None:
+        det["vs_default"] = round(ms / det["ms_per_step"], 4)
+        line["deterministic"] = det
     if decode is not None:
         line["decode_c2"] = {"what": "BASELINE config c2 on the same GPU and weights: full layer (router GEMM, "
                                      "routing, quantisation, grouped GEMMs, combine, shared expert) on the first T "
