@@ -381,8 +381,12 @@ __global__ void ep_pull_plan_kernel(PeerRegions reg, int rank, int world, int se
   }
 }
 
-// Block per received row (grid-stride): 16-byte loads from the source rank's
-// region, two in flight per thread, stored into the local receive rows.
+// Grid-stride over the 16-byte chunks of all received rows: each thread
+// issues kPullUnroll loads (from the source rank's region, over NVLink for a
+// peer) before its stores, so a CTA keeps 32 KB in flight; consecutive threads
+// take consecutive chunks of a row (coalesced on both sides).
+constexpr int kPullUnroll = 8;
+
 __global__ void __launch_bounds__(256) ep_pull_rows_kernel(PeerRegions reg, const int32_t* __restrict__ info,
                                                            int world, size_t rb, uint8_t* __restrict__ recv) {
   __shared__ int s_start[kMaxWorld + 1];
@@ -392,21 +396,30 @@ __global__ void __launch_bounds__(256) ep_pull_rows_kernel(PeerRegions reg, cons
   __syncthreads();
   const int R = info[kInfoR];
   const int n16 = static_cast<int>(rb / 16);
-  const int nt = blockDim.x;
-  for (int r = blockIdx.x; r < R; r += gridDim.x) {
-    int s = 0;
-    while (s + 1 < world && s_start[s + 1] <= r) ++s;
-    const uint4* src = reinterpret_cast<const uint4*>(reg.base[s] + kEpHdrBytes +
-                                                      (size_t)(s_off[s] + r - s_start[s]) * rb);
-    uint4* dst = reinterpret_cast<uint4*>(recv + (size_t)r * rb);
-    for (int c = threadIdx.x; c < n16; c += 2 * nt) {
-      const uint4 a = src[c];
-      const bool two = c + nt < n16;
-      uint4 b;
-      if (two) b = src[c + nt];
-      dst[c] = a;
-      if (two) dst[c + nt] = b;
+  const long long total = (long long)R * n16;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long base = (long long)blockIdx.x * blockDim.x + threadIdx.x; base < total;
+       base += stride * kPullUnroll) {
+    uint4 v[kPullUnroll];
+    uint4* dst[kPullUnroll];
+#pragma unroll
+    for (int u = 0; u < kPullUnroll; ++u) {
+      const long long i = base + u * stride;
+      dst[u] = nullptr;
+      if (i < total) {
+        const int r = static_cast<int>(i / n16);
+        const int c = static_cast<int>(i - (long long)r * n16);
+        int s = 0;
+        while (s + 1 < world && s_start[s + 1] <= r) ++s;
+        const uint4* src = reinterpret_cast<const uint4*>(reg.base[s] + kEpHdrBytes +
+                                                          (size_t)(s_off[s] + r - s_start[s]) * rb);
+        v[u] = src[c];
+        dst[u] = reinterpret_cast<uint4*>(recv + (size_t)r * rb) + c;
+      }
     }
+#pragma unroll
+    for (int u = 0; u < kPullUnroll; ++u)
+      if (dst[u]) *dst[u] = v[u];
   }
 }
 
