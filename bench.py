@@ -570,15 +570,22 @@ def gpu_arm(a):
                            deterministic=True, **kw1)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dev_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
+        for e3 in dev_evs:
+            for e in e3:
+                e.record()
+        torch.cuda.synchronize()
         e0.record()
-        for _ in range(a.steps):
+        for i in range(a.steps):
             gemms_b200.moe(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
-                           deterministic=True, **kw1)
+                           deterministic=True, profile_events=dev_evs[i], **kw1)
         e1.record()
         torch.cuda.synchronize()
         ms_det = e0.elapsed_time(e1) / a.steps
+        g2_det = statistics.mean(e3[1].elapsed_time(e3[2]) for e3 in dev_evs)
         det = {"what": "same c1 step with deterministic=True (per-token fixed-order combine, bit-reproducible)",
-               "ms_per_step": round(ms_det, 4), "tokens_per_s": round(base.T / (ms_det / 1e3), 1)}
+               "ms_per_step": round(ms_det, 4), "tokens_per_s": round(base.T / (ms_det / 1e3), 1),
+               "gemm2_ms": round(g2_det, 4)}
     clocks = sampler.stop() if sampler else None
 
     tokens_total = base.T
