@@ -289,6 +289,17 @@ class CudaEpKernels:
                    "gemms_ep_combine_peer")
         return out
 
+    def side_stream(self):
+        """A second stream of the current device (cached), for work that
+        overlaps the exchange."""
+        dev = torch.cuda.current_device()
+        key = ("side", dev)
+        st = self._ws.get(key)
+        if st is None:
+            st = torch.cuda.Stream(device=dev)
+            self._ws[key] = st
+        return st
+
     def exchange_flags(self, region) -> int:
         """info[2] of the last pull (reads the device: synchronises)."""
         return int(region.info[2].item())
@@ -425,15 +436,32 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     P_cap = recv_cap * min(top_k, E_local)
     reg = K.exchange_region(group, send_cap, recv_cap, H, top_k)
     send_counts, send_row_of, _, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local, region=reg)
+    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
     mark("pack")
+    # The shared expert needs only this rank's tokens: with a side stream it
+    # runs beside the barriers, the pull and the routed experts (its GEMMs
+    # leave GEMMS_EP_COMM_SMS SMs to the pull and NCCL), and the combine waits
+    # for it.
+    side = K.side_stream() if shared[0] is not None and _peer_overlap() else None
+    done_shared = None
+    if side is not None:
+        ready = torch.cuda.Event()
+        ready.record()
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            for t in (xq, xq_scale, acc):
+                t.record_stream(side)
+            with K.comm_overlap():
+                K.shared_ffn(xq, xq_scale, *shared, inter_planes, acc, 0)
+            done_shared = torch.cuda.Event()
+            done_shared.record()
     K.peer_barrier(group, reg)  # every rank's counts and send rows are written
     mark("publish_rows")
     recv_buf, info = K.pull(reg, rank, world, H, top_k)
     mark("pull")
-    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
-    if shared[0] is not None:
+    if shared[0] is not None and side is None:
         K.shared_ffn(xq, xq_scale, *shared, inter_planes, acc, 0)
-    mark("shared_ffn")
+        mark("shared_ffn")
     stats = _recv_stats(recv_buf, info, H, top_k, rank, E_local) if timeline is not None else None
     out_rows = K.expert_ffn_dev(recv_buf, info, reg.recv_cap, P_cap, H, I, top_k, E_local, rank * E_local,
                                 inter_planes, w13, w13_scale, w2, w2_scale)
@@ -442,10 +470,19 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     mark("pack_back")
     K.peer_barrier(group, reg)  # every rank's combine rows are written
     mark("publish")
+    if done_shared is not None:
+        torch.cuda.current_stream().wait_event(done_shared)
+        mark("shared_wait")
     out = K.combine_peer(acc, reg, info, send_row_of, world)
     mark("gather")
     _timeline_stats(timeline, stats)
     return out
+
+
+def _peer_overlap() -> bool:
+    """GEMMS_EP_PEER_OVERLAP=0 runs the shared expert in stream order instead
+    of on the side stream (exchange="peer")."""
+    return os.environ.get("GEMMS_EP_PEER_OVERLAP", "1") != "0"
 
 
 def _recv_stats(recv_buf, R, H, top_k, rank, E_local):

@@ -190,6 +190,9 @@ class CpuEpKernels:
     def exchange_flags(self, reg):
         return 0
 
+    def side_stream(self):
+        return None  # CPU: the shared expert runs in order
+
     @staticmethod
     def unpack_back(packed_row, H):
         vals = packed_row[:2 * H].contiguous().view(torch.float16).to(torch.float32)
