@@ -23,7 +23,8 @@ __device__ __forceinline__ uint32_t quant4(float v0, float v1, float v2, float v
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
-// One block of 8 warps per token; warp w handles 128-column blocks w, w+8, ...
+// Block (t, y) of 8 warps handles token t; warp w takes the 128-column blocks
+// y*8 + w, y*8 + w + 8*gridDim.y, ...
 // Each lane owns 4 consecutive columns of a block, so a warp writes one
 // 128-byte line per destination row.
 __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a) {
@@ -48,7 +49,7 @@ __global__ void __launch_bounds__(256) permute_kernel(PermuteArgs a) {
   const int* dst = s_dst;
   if (nd == 0) return;
   const int KB = a.H / kBlock;
-  for (int kb = warp; kb < KB; kb += 8) {
+  for (int kb = blockIdx.y * 8 + warp; kb < KB; kb += 8 * gridDim.y) {
     const size_t src = (size_t)t * a.H + (size_t)kb * kBlock + lane * 4;
     uint32_t packed;
     float scale;
@@ -208,7 +209,11 @@ __global__ void __launch_bounds__(256, 4) combine_slots_kernel(const float* __re
 int launch_permute(const PermuteArgs& a, cudaStream_t s) {
   if (a.T <= 0) return GEMMS_OK;
   if (a.top_k > 16) return GEMMS_ERR_SHAPE;
-  permute_kernel<<<a.T, 256, 0, s>>>(a);
+  // Few tokens (decode): split each token's 128-column blocks over several
+  // blocks, one column block per warp, so that the copy is not one block's
+  // serial loop.
+  const int col_blocks = a.T < 4 * num_sms() ? cdiv(a.H / kBlock, 8) : 1;
+  permute_kernel<<<dim3(a.T, col_blocks), 256, 0, s>>>(a);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

@@ -165,6 +165,159 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   }
 }
 
+// Decode-sized batches: one 256-thread block per token, thread e owns expert e
+// (E <= 256), so the token's dependency chain (group scores, group choice,
+// top-k) is spread over 8 warps instead of running in one.  Same arithmetic
+// as route_kernel and the same (value desc, index asc) order at every choice,
+// so the results are identical: each warp keeps its own top-k of the kept
+// candidates, and warp 0 picks the global top-k from those lists (the global
+// top-k under a strict order lies in the union of the warps' top-k).
+constexpr int kRouteBlockMaxT = 64;
+
+__global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
+  __shared__ float s_g[256];           // group scores (n_group <= E / 2)
+  __shared__ int s_kept[256];
+  __shared__ float s_v[8][16], s_s[8][16];
+  __shared__ int s_i[8][16];
+  const unsigned full = 0xffffffffu;
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int E = a.E, ng = a.n_group;
+  const int gs = E / ng;
+  const int e = tid;
+  const bool live = e < E;
+  float s = 0.f, sb = -INFINITY;
+  if (live) {
+    float x;
+    if (a.partials) {
+      const float* pp = a.partials + (size_t)t * E + e;
+      x = pp[0];
+      for (int q = 1; q < a.n_partials; ++q) x = __fadd_rn(x, pp[(size_t)q * a.T * E]);
+      if (a.logits_out) a.logits_out[(size_t)t * E + e] = x;
+    } else {
+      x = __ldg(a.logits + (size_t)t * E + e);
+    }
+    const float ex = static_cast<float>(exp(-static_cast<double>(x)));
+    s = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+    const float bias = a.bias_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[e])
+                                   : reinterpret_cast<const float*>(a.bias)[e];
+    sb = __fadd_rn(s, bias);
+  }
+  // group score: sum of the group's two largest biased scores (segmented butterfly)
+  Top2 t2{sb, -INFINITY};
+  for (int off = 1; off < gs; off <<= 1) {
+    Top2 o{__shfl_xor_sync(full, t2.a, off), __shfl_xor_sync(full, t2.b, off)};
+    t2 = merge_top2(t2, o);
+  }
+  if (live && e % gs == 0) s_g[e / gs] = __fadd_rn(t2.a, t2.b);
+  __syncthreads();
+  if (warp == 0) {  // the topk_group best groups
+    for (int g = lane; g < ng; g += 32) s_kept[g] = 0;
+    __syncwarp();
+    for (int it = 0; it < a.topk_group; ++it) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int g = lane; g < ng; g += 32)
+        if (!s_kept[g]) argmax_merge(bv, bi, s_g[g], g);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(full, bv, off);
+        const int oi = __shfl_xor_sync(full, bi, off);
+        argmax_merge(bv, bi, ov, oi);
+      }
+      if (lane == 0 && bi >= 0 && bi < ng) s_kept[bi] = 1;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // each warp: top-k of its 32 candidates
+  float cand = (live && s_kept[e / gs]) ? sb : -INFINITY;
+  for (int it = 0; it < a.top_k; ++it) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.f;
+    if (cand > bv) {
+      bv = cand;
+      bi = e;
+      bs = s;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(full, bv, off);
+      const int oi = __shfl_xor_sync(full, bi, off);
+      const float os = __shfl_xor_sync(full, bs, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    if (lane == 0) {
+      s_v[warp][it] = bv;
+      s_i[warp][it] = bi;
+      s_s[warp][it] = bs;
+    }
+    if (e == bi) cand = -INFINITY;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  // warp 0: the global top-k from the 8 lists (lane holds entries lane, lane+32, ...)
+  const int n = 8 * a.top_k;
+  bool taken[4] = {false, false, false, false};
+  int my_e = -1;
+  float my_s = 0.f;
+  for (int it = 0; it < a.top_k; ++it) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int m = lane + 32 * q;
+      if (m < n && !taken[q]) {
+        const float v = s_v[m / a.top_k][m % a.top_k];
+        const int i = s_i[m / a.top_k][m % a.top_k];
+        if (v > bv || (v == bv && v > -INFINITY && i < bi)) {
+          bv = v;
+          bi = i;
+          bs = s_s[m / a.top_k][m % a.top_k];
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(full, bv, off);
+      const int oi = __shfl_xor_sync(full, bi, off);
+      const float os = __shfl_xor_sync(full, bs, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    if (lane == it) {
+      my_e = bi;
+      my_s = bs;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int m = lane + 32 * q;
+      if (m < n && !taken[q] && bv > -INFINITY && s_i[m / a.top_k][m % a.top_k] == bi) taken[q] = true;
+    }
+  }
+  float sum = (lane < a.top_k) ? my_s : 0.f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(full, sum, off);
+  sum = __fadd_rn(sum, 1e-20f);
+  if (lane < a.top_k) {
+    const size_t o = (size_t)t * a.top_k + lane;
+    a.topk_idx[o] = my_e;
+    a.topk_w[o] = __fmul_rn(__fdiv_rn(my_s, sum), a.rsf);
+    if (a.pair_row) a.pair_row[o] = -1;
+    const int le = my_e - a.local_offset;
+    if (a.counts && le >= 0 && le < a.E_local) atomicAdd(a.counts + le, 1);
+  }
+}
+
 // Single block: per-group exclusive offsets and the 128-row M-tile list.
 __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
   __shared__ int s_tiles[1024];
@@ -298,6 +451,11 @@ int launch_sum_partials(const float* partials, int splits, int T, int E, float* 
 
 int launch_route(const RouteArgs& a, cudaStream_t s) {
   if (a.T <= 0) return GEMMS_OK;
+  if (a.T <= kRouteBlockMaxT && a.E <= 256 && a.top_k <= 16) {
+    route_block_kernel<<<a.T, 256, 0, s>>>(a);
+    GEMMS_CUDA_TRY(cudaGetLastError());
+    return GEMMS_OK;
+  }
   const int warps_per_block = 8;
   route_kernel<<<cdiv(a.T, warps_per_block), warps_per_block * 32, 0, s>>>(a);
   GEMMS_CUDA_TRY(cudaGetLastError());

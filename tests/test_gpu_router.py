@@ -104,3 +104,22 @@ def test_router_gemm_small_expert_count():
     ref = R.router_logits(x, rw)
     assert _logits_err(got, ref) <= 1e-5
     torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5 * float(ref.abs().max()))
+
+
+@pytest.mark.parametrize("E,ng,tg,k", [(256, 8, 4, 8), (64, 32, 4, 4), (128, 8, 3, 6), (256, 16, 8, 16), (32, 2, 1, 3),
+                                       (16, 4, 2, 2), (256, 128, 16, 8)])
+def test_router_small_batch_kernel_matches_large_batch_kernel(E, ng, tg, k):
+    """Batches of <= 64 tokens go through the block-per-token router, larger
+    ones through the warp-per-token router; routing is per token, so the
+    first 48 tokens routed alone must give exactly what they give inside a
+    batch of 300 (ids, weights, counts)."""
+    g = torch.Generator().manual_seed(E + 13 * k)
+    logits = (torch.randn(300, E, generator=g) * 2).cuda()
+    bias = ((torch.rand(E, generator=g) - 0.5) * 0.2).cuda()
+    idx_l, w_l, _ = gemms_b200.route(logits, bias, n_group=ng, topk_group=tg, top_k=k, routed_scaling_factor=2.5)
+    idx_s, w_s, c_s = gemms_b200.route(logits[:48].contiguous(), bias, n_group=ng, topk_group=tg, top_k=k,
+                                       routed_scaling_factor=2.5)
+    torch.cuda.synchronize()
+    assert torch.equal(idx_s, idx_l[:48])
+    assert torch.equal(w_s, w_l[:48])
+    assert torch.equal(c_s.cpu().long(), torch.bincount(idx_s.reshape(-1).cpu().long(), minlength=E))
