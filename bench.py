@@ -53,7 +53,7 @@ def _args():
     p.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
     p.add_argument("--ep-exchange", choices=["nccl", "peer"], default=None,
                    help="N>1: rows exchanged by NCCL all-to-all or device-driven over symmetric memory "
-                        "(default: GEMMS_EP_EXCHANGE, else nccl)")
+                        "(default: GEMMS_EP_EXCHANGE, else peer)")
     return p.parse_args()
 
 
@@ -263,7 +263,7 @@ def config_dict(cfg, base, sh, n_local, planes, world, zipf_hist=None):
                       f"groups {sh.n_group}/{sh.topk_group} top-{sh.top_k}" + (" + shared expert" if sh.shared else "")),
          "tokens_per_rank": sh.T, "experts_per_rank": n_local, "inter_planes": planes,
          "parallelism": f"ep{world}" if world > 1 else "single GPU",
-         **({"ep_exchange": os.environ.get("GEMMS_EP_EXCHANGE", "nccl")} if world > 1 else {}),
+         **({"ep_exchange": os.environ.get("GEMMS_EP_EXCHANGE", "peer")} if world > 1 else {}),
          "l2": "inputs larger than L2 (11.3 GB of expert weights streamed per step)"}
     if zipf_hist is not None:
         per_rank = zipf_hist.reshape(8, -1).sum(1)
@@ -426,8 +426,9 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 8, 32, 128), steps=50, warmup=5):
 
 
 def gpu_arm(a):
-    if a.ep_exchange:
-        os.environ["GEMMS_EP_EXCHANGE"] = a.ep_exchange
+    # N>1 default: the device-driven exchange (no host synchronisation; every
+    # rank runs the same token count here)
+    os.environ["GEMMS_EP_EXCHANGE"] = a.ep_exchange or os.environ.get("GEMMS_EP_EXCHANGE") or "peer"
     import torch
     import torch.distributed as dist
 

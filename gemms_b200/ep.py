@@ -438,10 +438,10 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     send_counts, send_row_of, _, xq, xq_scale = K.dispatch(idx, wts, x, world, E_local, region=reg)
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
     mark("pack")
-    # The shared expert needs only this rank's tokens: with a side stream it
-    # runs beside the barriers, the pull and the routed experts (its GEMMs
-    # leave GEMMS_EP_COMM_SMS SMs to the pull and NCCL), and the combine waits
-    # for it.
+    # The shared expert needs only this rank's tokens: optionally it runs on a
+    # side stream beside the barriers, the pull and the routed experts (its
+    # GEMMs leave GEMMS_EP_COMM_SMS SMs to the pull and NCCL), and the combine
+    # waits for it.
     side = K.side_stream() if shared[0] is not None and _peer_overlap() else None
     done_shared = None
     if side is not None:
@@ -480,9 +480,11 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
 
 
 def _peer_overlap() -> bool:
-    """GEMMS_EP_PEER_OVERLAP=0 runs the shared expert in stream order instead
-    of on the side stream (exchange="peer")."""
-    return os.environ.get("GEMMS_EP_PEER_OVERLAP", "1") != "0"
+    """GEMMS_EP_PEER_OVERLAP=1 runs the shared expert on a side stream beside
+    the exchange (exchange="peer").  Off by default: at N=2 (c3) the shared
+    GEMMs only took SMs from the routed experts' GEMMs (14.45 vs 14.37 ms per
+    step), since the exchange itself leaves little idle time to fill."""
+    return os.environ.get("GEMMS_EP_PEER_OVERLAP", "0") == "1"
 
 
 def _recv_stats(recv_buf, R, H, top_k, rank, E_local):
