@@ -64,6 +64,7 @@ struct PlanArgs {
   int32_t* tile_row0;
   int32_t* tile_rows;
   int32_t* num_tiles;     // [1]
+  int32_t* group_tile0;   // [groups + 1] first M tile of each group (+ total), optional
   int max_tiles;
   int row_capacity;       // grouped rows the buffers hold: more rows -> error word, no tiles
   int* err;
@@ -118,6 +119,7 @@ struct GemmGroupsArgs {
   const int32_t* tile_row0;
   const int32_t* tile_rows;
   const int32_t* num_tiles;
+  const int32_t* group_tile0;  // [groups + 1] (plan_kernel): lets the GEMMs order units expert by expert
   int max_tiles;
   int shared_group;  // group index that uses the shared expert's weights (-1: none)
 };

@@ -453,7 +453,7 @@ EpFfnLayout ep_ffn_layout(int R_max, int P_max, int H, int I, int E_local, int t
   L.err = take(64);
   L.counts = take(sizeof(int32_t) * std::max(E_local, 1));
   L.head = o;
-  L.offsets = take(sizeof(int32_t) * (E_local + 1));
+  L.offsets = take(sizeof(int32_t) * 2 * (E_local + 1));  // offsets, then first tile per group
   L.tile_group = take(sizeof(int32_t) * L.max_tiles);
   L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
   L.tile_rows = take(sizeof(int32_t) * L.max_tiles);
@@ -558,6 +558,7 @@ int ep_expert_ffn_impl(const void* recv_buf, int32_t R, const int32_t* R_dev, in
   pa.tile_row0 = at<int32_t>(ws, L.tile_row0);
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
+  pa.group_tile0 = pa.offsets + (E_local + 1);
   pa.max_tiles = L.max_tiles;
   pa.row_capacity = L.P;
   pa.err = err;
@@ -604,6 +605,7 @@ int ep_expert_ffn_impl(const void* recv_buf, int32_t R, const int32_t* R_dev, in
   gg.tile_row0 = pa.tile_row0;
   gg.tile_rows = pa.tile_rows;
   gg.num_tiles = pa.num_tiles;
+  gg.group_tile0 = pa.group_tile0;
   gg.max_tiles = L.max_tiles;
   gg.shared_group = -1;
   const int P = L.P;

@@ -33,6 +33,7 @@
 #include <atomic>
 #include <cudaTypedefs.h>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace gemms {
@@ -79,6 +80,7 @@ struct GemmParams {
   const int32_t* tile_row0;
   const int32_t* tile_rows;
   const int32_t* num_tiles;
+  const int32_t* group_tile0;  // set: units ordered expert by expert, M tiles fastest (see unit_tile)
   int max_tiles;
   int shared_group;
   int n_tiles;       // N tiles per M tile
@@ -112,6 +114,26 @@ struct GemmParams {
   long long wait_limit;
   int stall_iter;
 };
+
+// Unit u -> (M tile, N tile).  Default: N fastest (consecutive CTAs share an A
+// tile).  With group_tile0: within an expert, its M tiles are fastest, so the
+// CTAs that read the same weight tile (one per M tile of the expert) run side
+// by side and the second read finds the tile in L2.  The units of group g are
+// [first_tile(g), first_tile(g + 1)) x n_tiles in either order.
+__device__ __forceinline__ void unit_tile(const GemmParams& p, int u, int num_tiles, int& mt, int& nt) {
+  const int mt0 = u / p.n_tiles;
+  if (!p.group_tile0) {
+    mt = mt0;
+    nt = u - mt0 * p.n_tiles;
+    return;
+  }
+  const int g = p.tile_group[mt0];
+  const int t0 = p.group_tile0[g];
+  const int c = min(p.group_tile0[g + 1], num_tiles) - t0;  // tiles of g that are listed
+  const int v = u - t0 * p.n_tiles;
+  mt = t0 + v % c;
+  nt = v / c;
+}
 
 __device__ __forceinline__ uint16_t f2_to_e4m3x2(float a, float b) {
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
@@ -194,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = it / p.kb_count;
         kb = it - i * p.kb_count;
         const int u = blockIdx.x + i * gridDim.x;
-        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        int mt, nt;
+        unit_tile(p, u, num_tiles, mt, nt);
         const int g = p.tile_group[mt];
         const bool sh = (g == p.shared_group);
         mb = sh ? &tmBs : &tmB;
@@ -209,7 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int it = 0;
       for (int u = blockIdx.x; u < total; u += gridDim.x) {
-        const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+        int mt, nt;
+        unit_tile(p, u, num_tiles, mt, nt);
         const int g = p.tile_group[mt], row0 = p.tile_row0[mt];
         const bool sh = (g == p.shared_group);
         const CUtensorMap* mb = sh ? &tmBs : &tmB;
@@ -325,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc_it = 0, unit_i = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++unit_i) {
-      const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+      int mt, nt;
+      unit_tile(p, u, num_tiles, mt, nt);
       const int g = p.tile_group[mt], row0 = p.tile_row0[mt], rows = p.tile_rows[mt];
       const bool valid = r < rows;
       const float* ws = (g == p.shared_group) ? p.sw_scale : p.w_scale + (size_t)g * wblk * p.kb_count;
@@ -530,6 +555,16 @@ void apply_wait_knobs(GemmParams& p, int gemm) {
 // Weight K-blocks a CTA keeps in flight toward L2 beyond its smem ring.  The
 // weight stream is DRAM-latency bound (one 32 KB stage per K-block per SM);
 // GEMMS_PREFETCH overrides the default for tuning.
+// Unit order of the grouped GEMMs: GEMMS_GEMM_UNIT_ORDER=expert puts an
+// expert's M tiles side by side (see unit_tile); default: N tiles fastest.
+bool expert_unit_order() {
+  static const bool v = [] {
+    const char* e = std::getenv("GEMMS_GEMM_UNIT_ORDER");
+    return e && std::strcmp(e, "expert") == 0;
+  }();
+  return v;
+}
+
 int prefetch_depth() {
   static int depth = -1;
   if (depth < 0) {
@@ -618,6 +653,7 @@ int launch_gemm1(const Gemm1Args& a, cudaStream_t s) {
   p.b_row_step = kBlock;
   p.b_row_hi = a.I;
   p.prefetch = prefetch_depth();
+  p.group_tile0 = expert_unit_order() ? a.g.group_tile0 : nullptr;
   p.a_scale = a.a_scale;
   p.a_scale_ld = a.a_scale_ld;
   p.w_scale = a.w13_scale;
@@ -660,6 +696,7 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s) {
   p.b_row_step = BN;
   p.b_row_hi = kBlock;
   p.prefetch = prefetch_depth();
+  p.group_tile0 = expert_unit_order() ? a.g.group_tile0 : nullptr;
   p.a_scale = a.inter_scale;
   p.a_scale_ld = a.inter_scale_ld;
   p.w_scale = a.w2_scale;

@@ -48,7 +48,7 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.topk_idx = take(sizeof(int32_t) * (size_t)L.T * L.K);
   L.topk_w = take(sizeof(float) * (size_t)L.T * L.K);
   L.pair_row = take(sizeof(int32_t) * (size_t)L.T * L.K);
-  L.offsets = take(sizeof(int32_t) * (L.groups + 1));
+  L.offsets = take(sizeof(int32_t) * 2 * (L.groups + 1));  // offsets, then first tile per group
   L.tile_group = take(sizeof(int32_t) * L.max_tiles);
   L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
   L.tile_rows = take(sizeof(int32_t) * L.max_tiles);
@@ -212,6 +212,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   pa.tile_row0 = at<int32_t>(ws, L.tile_row0);
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
+  pa.group_tile0 = pa.offsets + (L.groups + 1);
   pa.max_tiles = L.max_tiles;
   pa.row_capacity = L.R_max;
   pa.err = err;
@@ -252,6 +253,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   gg.tile_row0 = pa.tile_row0;
   gg.tile_rows = pa.tile_rows;
   gg.num_tiles = pa.num_tiles;
+  gg.group_tile0 = pa.group_tile0;
   gg.max_tiles = L.max_tiles;
   gg.shared_group = L.shared ? s.E_local : -1;
 
@@ -395,7 +397,7 @@ FfnLayout ffn_layout(int R_max, int H, int I, int E_local, int planes) {
     return at;
   };
   L.err = take(64);
-  L.offsets = take(sizeof(int32_t) * (L.groups + 1));
+  L.offsets = take(sizeof(int32_t) * 2 * (L.groups + 1));  // offsets, then first tile per group
   L.tile_group = take(sizeof(int32_t) * L.max_tiles);
   L.tile_row0 = take(sizeof(int32_t) * L.max_tiles);
   L.tile_rows = take(sizeof(int32_t) * L.max_tiles);
@@ -448,6 +450,7 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
   pa.tile_row0 = at<int32_t>(ws, L.tile_row0);
   pa.tile_rows = at<int32_t>(ws, L.tile_rows);
   pa.num_tiles = at<int32_t>(ws, L.num_tiles);
+  pa.group_tile0 = pa.offsets + (L.groups + 1);
   pa.max_tiles = L.max_tiles;
   pa.row_capacity = std::max(R_max, 1);
   pa.err = err;
@@ -458,6 +461,7 @@ int gemms_expert_ffn(const void* rows_fp8, const float* rows_scale, int32_t R_ma
   gg.tile_row0 = pa.tile_row0;
   gg.tile_rows = pa.tile_rows;
   gg.num_tiles = pa.num_tiles;
+  gg.group_tile0 = pa.group_tile0;
   gg.max_tiles = L.max_tiles;
   gg.shared_group = -1;
 

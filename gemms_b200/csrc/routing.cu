@@ -349,6 +349,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     const int tile0 = tiles_total + incl_t - (c + kBlock - 1) / kBlock;
     if (g < groups) {
       a.offsets[g] = row0;
+      if (a.group_tile0) a.group_tile0[g] = tile0;
       const int nt = (c + kBlock - 1) / kBlock;
       for (int i = 0; i < nt; ++i) {
         const int ti = tile0 + i;
@@ -367,6 +368,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
   }
   if (tid == 0) {
     a.offsets[groups] = rows_total;
+    if (a.group_tile0) a.group_tile0[groups] = tiles_total;
     a.num_tiles[0] = min(tiles_total, a.max_tiles);
     if (rows_total > a.row_capacity) {  // counts disagree with the buffers' size: do no GEMM work
       a.num_tiles[0] = 0;
