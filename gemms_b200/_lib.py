@@ -23,6 +23,7 @@ GEMMS_INPUT_FP8 = 1
 EXPORTS = (
     "gemms_moe_workspace_size",
     "gemms_moe_fwd",
+    "gemms_set_decode_max_t",
     "gemms_route",
     "gemms_expert_ffn_workspace_size",
     "gemms_expert_ffn",
@@ -150,6 +151,8 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                           c_void_p]
         L.gemms_ep_expert_ffn.restype = c_int32
+        L.gemms_set_decode_max_t.argtypes = [c_int32]
+        L.gemms_set_decode_max_t.restype = c_int32
         L.gemms_set_gemm_ctas.argtypes = [c_int32]
         L.gemms_set_gemm_ctas.restype = c_int32
         L.gemms_ep_back_row_bytes.argtypes = [c_int32]

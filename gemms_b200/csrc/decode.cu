@@ -1,0 +1,337 @@
+// decode.cu -- the two expert GEMMs for decode-sized batches (T <= 4) on the
+// CUDA cores.
+//
+// With at most 4 rows per expert the tensor-core GEMMs (grouped_gemm.cu) run
+// each M tile as one long chain of 128-deep K blocks per CTA, MMA -> TMEM ->
+// promotion -> MMA, and at T=1 that chain, not HBM, sets their time (GEMM1:
+// one 56-block chain per CTA).  Here the work is a weight stream: every weight
+// byte is read once, converted from e4m3 and multiplied into <= 4 activation
+// rows held in shared memory, with many 16-byte loads in flight per SM, so the
+// time is the HBM time of the weights of the experts hit.
+//
+// Same operands and block-scale semantics as the tensor path (the reference's
+// dequantise-then-matmul, flashinfer_baseline.py:68-93, 154-169): per
+// 128-wide K block, sum(a_q * w_q) * a_scale[row, kb] * w_scale[n/128, kb],
+// accumulated in fp32.  GEMM1 applies SwiGLU (silu on the second half,
+// :157-160) and keeps the intermediate in fp32 (the reference's own precision;
+// the tensor path re-quantises it to two e4m3 planes for its FP8 GEMM2).
+// GEMM2 multiplies by the routing weight and adds into the token's fp32
+// output row (or stores the row for the deterministic combine).
+//
+// Work: the M-tile list of plan_kernel (one tile per hit expert, since rows
+// <= 4 < 128); a unit is (tile, a chunk of output rows); each CTA takes a
+// contiguous range of units, so it re-stages the activation rows only when the
+// tile changes.  Shared memory holds the activation rows as fp32 in a
+// [row][element-in-chunk][chunk] layout: lane c of a warp reads chunk c, so a
+// warp's shared loads hit 32 consecutive words (no bank conflicts).
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <algorithm>
+#include <atomic>
+
+namespace gemms {
+namespace {
+
+constexpr int kDecThreads = 512;   // 16 warps
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kChunk = 16;         // weights per 16-byte load
+constexpr int kRowsPerWarp = 4;    // GEMM1: 2 gate/up pairs; GEMM2: 4 output rows
+
+__device__ __forceinline__ void e4m3x16_to_f(const uint4& w, float* f) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+          static_cast<__nv_fp8x2_storage_t>((u[q] >> (16 * h)) & 0xffffu), __NV_E4M3);
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+      f[4 * q + 2 * h] = v.x;
+      f[4 * q + 2 * h + 1] = v.y;
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Contiguous unit range of this CTA.
+__device__ __forceinline__ void unit_range(int total, int& u0, int& u1) {
+  const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+  u0 = min(total, (int)blockIdx.x * per);
+  u1 = min(total, u0 + per);
+}
+
+// GEMM1 + SwiGLU.  Unit = (tile, 32 intermediate columns j); warp w takes
+// columns j0 + 2w and j0 + 2w + 1 (their gate rows j and up rows j + I).
+template <int MR>
+__global__ void __launch_bounds__(kDecThreads) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter) {
+  extern __shared__ float smem[];
+  const int H = a.H, I = a.I, KB = H / kBlock, NC = H / kChunk;
+  float* sA = smem;                        // [MR][16][NC]
+  float* sS = smem + (size_t)MR * H;       // [MR][KB] activation scales
+  const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
+  const int per_tile = I / (2 * kDecWarps);
+  int u0, u1;
+  unit_range(num_tiles * per_tile, u0, u1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int staged = -1;
+  for (int u = u0; u < u1; ++u) {
+    const int tile = u / per_tile, jc = u - tile * per_tile;
+    const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
+    if (tile != staged) {
+      __syncthreads();  // previous tile's rows no longer read
+      for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
+        const int r = i / NC, c = i - r * NC;
+        float f[kChunk];
+        if (r < rows) {
+          e4m3x16_to_f(*reinterpret_cast<const uint4*>(a.a + (size_t)(row0 + r) * H + (size_t)c * kChunk), f);
+        } else {
+#pragma unroll
+          for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
+      }
+      for (int i = threadIdx.x; i < MR * KB; i += blockDim.x) {
+        const int r = i / KB, kb = i - r * KB;
+        sS[i] = r < rows ? a.a_scale[(size_t)kb * a.a_scale_ld + row0 + r] : 0.f;
+      }
+      __syncthreads();
+      staged = tile;
+    }
+    const bool sh = g == a.g.shared_group;
+    const uint8_t* W = sh ? a.sw13 : a.w13 + (size_t)g * 2 * I * H;
+    const float* WS = sh ? a.sw13_scale : a.w13_scale + (size_t)g * (2 * I / kBlock) * KB;
+    const int j0 = jc * 2 * kDecWarps + 2 * warp;
+    // weight rows: gate j0, gate j0+1, up j0, up j0+1
+    const uint8_t* wrow[kRowsPerWarp] = {W + (size_t)j0 * H, W + (size_t)(j0 + 1) * H, W + (size_t)(I + j0) * H,
+                                         W + (size_t)(I + j0 + 1) * H};
+    const float* wsc[kRowsPerWarp] = {WS + (size_t)(j0 / kBlock) * KB, WS + (size_t)((j0 + 1) / kBlock) * KB,
+                                      WS + (size_t)((I + j0) / kBlock) * KB,
+                                      WS + (size_t)((I + j0 + 1) / kBlock) * KB};
+    float acc[kRowsPerWarp][MR];
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
+    // two chunks of loads in flight per lane: the next chunk's weights are
+    // requested before this chunk's arithmetic
+    uint4 wv[kRowsPerWarp], wn[kRowsPerWarp];
+    if (lane < NC) {
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ldg_stream(wrow[q] + (size_t)lane * kChunk);
+    }
+    for (int c = lane; c < NC; c += 32) {
+      if (c + 32 < NC) {
+#pragma unroll
+        for (int q = 0; q < kRowsPerWarp; ++q) wn[q] = ldg_stream(wrow[q] + (size_t)(c + 32) * kChunk);
+      }
+      const int kb = c / (kBlock / kChunk);
+      float part[kRowsPerWarp][MR];
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+        for (int r = 0; r < MR; ++r) part[q][r] = 0.f;
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) {
+        float f[kChunk];
+        e4m3x16_to_f(wv[q], f);
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e)
+#pragma unroll
+          for (int r = 0; r < MR; ++r) part[q][r] = fmaf(f[e], sA[((size_t)r * kChunk + e) * NC + c], part[q][r]);
+      }
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) {
+        const float ws = __ldg(wsc[q] + kb);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[q][r], sS[r * KB + kb] * ws, acc[q][r]);
+      }
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = wn[q];
+    }
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
+    if (lane < 2 * MR) {  // lane = (column j0 + (lane & 1), row lane >> 1)
+      const int jj = lane & 1, r = lane >> 1;
+      float gate = 0.f, up = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < MR; ++rr)
+        if (rr == r) {
+          gate = jj ? acc[1][rr] : acc[0][rr];
+          up = jj ? acc[3][rr] : acc[2][rr];
+        }
+      if (r < rows) inter[(size_t)(row0 + r) * I + j0 + jj] = up * sm100::rcp_approx(1.0f + __expf(-up)) * gate;
+    }
+  }
+}
+
+// GEMM2 + routing weight.  Unit = (tile, 64 output columns h); warp w takes
+// h0 + 4w .. h0 + 4w + 3.
+template <int MR>
+__global__ void __launch_bounds__(kDecThreads) decode_gemm2_kernel(Gemm2Args a, const float* __restrict__ inter) {
+  extern __shared__ float smem[];
+  const int H = a.H, I = a.I, KB = I / kBlock, NC = I / kChunk;
+  float* sC = smem;  // [MR][16][NC]
+  const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
+  const int per_tile = H / (kRowsPerWarp * kDecWarps);
+  int u0, u1;
+  unit_range(num_tiles * per_tile, u0, u1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int staged = -1;
+  for (int u = u0; u < u1; ++u) {
+    const int tile = u / per_tile, hc = u - tile * per_tile;
+    const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
+    if (tile != staged) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < MR * I; i += blockDim.x) {
+        const int r = i / I, k = i - r * I;  // consecutive threads: consecutive k (coalesced global reads)
+        const int c = k / kChunk, e = k - c * kChunk;
+        sC[((size_t)r * kChunk + e) * NC + c] = r < rows ? inter[(size_t)(row0 + r) * I + k] : 0.f;
+      }
+      __syncthreads();
+      staged = tile;
+    }
+    const bool sh = g == a.g.shared_group;
+    const uint8_t* W = sh ? a.sw2 : a.w2 + (size_t)g * H * I;
+    const float* WS = sh ? a.sw2_scale : a.w2_scale + (size_t)g * (H / kBlock) * KB;
+    const int h0 = hc * kRowsPerWarp * kDecWarps + kRowsPerWarp * warp;
+    float acc[kRowsPerWarp][MR];
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
+    uint4 wv[kRowsPerWarp], wn[kRowsPerWarp];
+    if (lane < NC) {
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ldg_stream(W + (size_t)(h0 + q) * I + (size_t)lane * kChunk);
+    }
+    for (int c = lane; c < NC; c += 32) {
+      if (c + 32 < NC) {
+#pragma unroll
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          wn[q] = ldg_stream(W + (size_t)(h0 + q) * I + (size_t)(c + 32) * kChunk);
+      }
+      const int kb = c / (kBlock / kChunk);
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) {
+        float f[kChunk];
+        e4m3x16_to_f(wv[q], f);
+        float part[MR];
+#pragma unroll
+        for (int r = 0; r < MR; ++r) part[r] = 0.f;
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e)
+#pragma unroll
+          for (int r = 0; r < MR; ++r) part[r] = fmaf(f[e], sC[((size_t)r * kChunk + e) * NC + c], part[r]);
+        const float ws = __ldg(WS + (size_t)((h0 + q) / kBlock) * KB + kb);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[r], ws, acc[q][r]);
+      }
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = wn[q];
+    }
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
+    if (lane < kRowsPerWarp * MR) {  // lane = (column h0 + (lane % 4), row lane / 4)
+      const int q = lane % kRowsPerWarp, r = lane / kRowsPerWarp;
+      float v = 0.f;
+#pragma unroll
+      for (int qq = 0; qq < kRowsPerWarp; ++qq)
+#pragma unroll
+        for (int rr = 0; rr < MR; ++rr)
+          if (qq == q && rr == r) v = acc[qq][rr];
+      if (r < rows) {
+        const int row = row0 + r;
+        v *= a.row_weight[row];
+        if (a.pair_out)
+          a.pair_out[(size_t)row * H + h0 + q] = v;
+        else
+          atomicAdd(a.out + (size_t)a.row_dest[row] * H + h0 + q, v);
+      }
+    }
+  }
+}
+
+// Dynamic shared memory above 48 KB needs a per-device opt-in per kernel; the
+// bound is the largest size shape_ok admits.
+constexpr int kDecSmemMax = 200 * 1024;
+
+template <class K>
+int allow_smem(K kernel, std::atomic<uint32_t>& done) {
+  int dev = 0;
+  GEMMS_CUDA_TRY(cudaGetDevice(&dev));
+  const uint32_t bit = 1u << (dev & 31);
+  if (!(done.load() & bit)) {
+    GEMMS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemMax));
+    done.fetch_or(bit);
+  }
+  return GEMMS_OK;
+}
+
+template <int MR>
+int launch_gemm1_mr(const Gemm1Args& g1, float* inter, cudaStream_t s) {
+  static std::atomic<uint32_t> done{0};
+  const size_t smem = sizeof(float) * ((size_t)MR * g1.H + (size_t)MR * (g1.H / kBlock));
+  int rc;
+  if ((rc = allow_smem(decode_gemm1_kernel<MR>, done))) return rc;
+  // one CTA of 16 warps per SM (its registers fill the SM's file), each
+  // keeping two chunks of four weight rows in flight per lane
+  decode_gemm1_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g1, inter);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+template <int MR>
+int launch_gemm2_mr(const Gemm2Args& g2, const float* inter, cudaStream_t s) {
+  static std::atomic<uint32_t> done{0};
+  const size_t smem = sizeof(float) * (size_t)MR * g2.I;
+  int rc;
+  if ((rc = allow_smem(decode_gemm2_kernel<MR>, done))) return rc;
+  decode_gemm2_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g2, inter);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int shape_ok(int H, int I) {
+  return H % (kRowsPerWarp * kDecWarps) == 0 && I % (2 * kDecWarps) == 0 && H % kBlock == 0 && I % kBlock == 0 &&
+         (size_t)kDecodeMaxRows * (H + H / kBlock) * sizeof(float) <= (size_t)kDecSmemMax &&
+         (size_t)kDecodeMaxRows * I * sizeof(float) <= (size_t)kDecSmemMax;
+}
+
+}  // namespace
+
+int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, cudaStream_t s) {
+  if (max_rows < 1 || max_rows > kDecodeMaxRows || !shape_ok(g1.H, g1.I)) return GEMMS_ERR_SHAPE;
+  if (max_rows == 1) return launch_gemm1_mr<1>(g1, inter, s);
+  if (max_rows == 2) return launch_gemm1_mr<2>(g1, inter, s);
+  return launch_gemm1_mr<4>(g1, inter, s);
+}
+
+int launch_decode_gemm2(const Gemm2Args& g2, const float* inter, int max_rows, cudaStream_t s) {
+  if (max_rows < 1 || max_rows > kDecodeMaxRows || !shape_ok(g2.H, g2.I)) return GEMMS_ERR_SHAPE;
+  if (max_rows == 1) return launch_gemm2_mr<1>(g2, inter, s);
+  if (max_rows == 2) return launch_gemm2_mr<2>(g2, inter, s);
+  return launch_gemm2_mr<4>(g2, inter, s);
+}
+
+bool decode_shape_ok(int H, int I) { return shape_ok(H, I); }
+
+}  // namespace gemms

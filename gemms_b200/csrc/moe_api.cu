@@ -7,6 +7,9 @@
 // come back as GEMMS_ERR_* codes.
 #include "common.cuh"
 
+#include <atomic>
+#include <cstdlib>
+
 #include <algorithm>
 
 namespace gemms {
@@ -18,10 +21,22 @@ struct FwdLayout {
   size_t err, counts, topk_idx, topk_w, pair_row, offsets, tile_group, tile_row0, tile_rows, num_tiles;
   size_t row_token, row_weight, a_rows, a_scale, inter, inter_scale, out_acc, pair_out, total;
   int det;  // deterministic combine: per-row results in pair_out, summed per token in slot order
+  int decode_rows;  // > 0: expert GEMMs on the CUDA cores (decode.cu) for tiles of <= decode_rows rows
+  size_t dec_inter;  // fp32 SwiGLU output [R_max, I] of the decode path
   RouterPlan router;
   size_t router_planes, router_partials;  // router GEMM scratch (GEMMS_INPUT_BF16 only)
   size_t head_bytes;  // [0, head_bytes) is zeroed each call (error word + counts)
 };
+
+// Largest batch that takes the CUDA-core expert GEMMs: GEMMS_DECODE_MAX_T at
+// load time (default 4 = kDecodeMaxRows; 0 keeps every batch on the tensor
+// cores), changed by gemms_set_decode_max_t.
+std::atomic<int> g_decode_t_limit{[] {
+  const char* e = std::getenv("GEMMS_DECODE_MAX_T");
+  const int x = e ? std::atoi(e) : kDecodeMaxRows;
+  return std::max(0, std::min(x, kDecodeMaxRows));
+}()};
+int decode_t_limit() { return g_decode_t_limit.load(std::memory_order_relaxed); }
 
 FwdLayout fwd_layout(const GemmsMoeShape& s) {
   FwdLayout L{};
@@ -59,6 +74,10 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.a_scale = take(sizeof(float) * (size_t)(L.H / kBlock) * L.scale_ld);
   L.inter = take((size_t)std::max(L.R_max, 1) * L.planes * L.I);
   L.inter_scale = take(sizeof(float) * (size_t)(L.I / kBlock) * L.scale_ld);
+  L.decode_rows = 0;
+  if (s.T >= 1 && s.T <= decode_t_limit() && decode_shape_ok(s.H, s.I))
+    L.decode_rows = s.T <= 1 ? 1 : (s.T <= 2 ? 2 : 4);  // tiles hold <= T rows (routed and shared)
+  if (L.decode_rows) L.dec_inter = take(sizeof(float) * (size_t)std::max(L.R_max, 1) * L.I);
   L.det = s.deterministic ? 1 : 0;
   if (L.det)
     L.pair_out = take(sizeof(float) * (size_t)std::max(L.R_max, 1) * L.H);
@@ -128,6 +147,11 @@ const char* gemms_strerror(int code) {
     case GEMMS_ERR_CAPACITY: return "size exceeds a fixed capacity of this entry point";
     default: return "unknown error";
   }
+}
+
+int gemms_set_decode_max_t(int32_t max_t) {
+  if (max_t < 0) return GEMMS_ERR_ARG;
+  return gemms::g_decode_t_limit.exchange(std::min<int>(max_t, gemms::kDecodeMaxRows));
 }
 
 size_t gemms_moe_workspace_size(const GemmsMoeShape* shape) {
@@ -277,8 +301,9 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   g1.err = err;
   if (!g1.w13) g1.w13 = g1.sw13;
   cudaEvent_t const* evs = reinterpret_cast<cudaEvent_t const*>(args->profile_events);
+  float* dec_inter = L.decode_rows ? at<float>(ws, L.dec_inter) : nullptr;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[0], st));
-  if ((rc = launch_gemm1(g1, st))) return rc;
+  if ((rc = L.decode_rows ? launch_decode_gemm1(g1, dec_inter, L.decode_rows, st) : launch_gemm1(g1, st))) return rc;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[1], st));
 
   Gemm2Args g2{};
@@ -301,7 +326,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   g2.pair_out = L.det ? at<float>(ws, L.pair_out) : nullptr;
   g2.err = err;
   if (!g2.w2) g2.w2 = g2.sw2;
-  if ((rc = launch_gemm2(g2, st))) return rc;
+  if ((rc = L.decode_rows ? launch_decode_gemm2(g2, dec_inter, L.decode_rows, st) : launch_gemm2(g2, st))) return rc;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[2], st));
 
   if (L.det) {

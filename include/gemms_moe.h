@@ -112,6 +112,15 @@ typedef struct {
 /* Bytes of device workspace gemms_moe_fwd needs for this shape. */
 size_t gemms_moe_workspace_size(const GemmsMoeShape* shape);
 
+/* Batches of at most max_t tokens (<= 4) run the two expert GEMMs on the CUDA
+ * cores as weight streams (with <= 4 rows per expert the tensor-core GEMMs are
+ * bound by their per-K-block chain, not by HBM); 0 keeps every batch on the
+ * tensor cores.  Default 4, or GEMMS_DECODE_MAX_T at library load.  The
+ * workspace size depends on it: query gemms_moe_workspace_size after setting
+ * it.  Returns the previous value, or GEMMS_ERR_ARG if negative.  No
+ * counterpart in the reference. */
+int gemms_set_decode_max_t(int32_t max_t);
+
 /* Full layer forward: route -> permute(+quant) -> GEMM1+SwiGLU -> GEMM2 ->
  * weighted combine (+ shared expert) -> bf16.  Workspace must be 256-byte
  * aligned and at least gemms_moe_workspace_size() bytes; the contents need no
