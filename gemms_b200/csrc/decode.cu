@@ -53,13 +53,24 @@ __device__ __forceinline__ void e4m3x16_to_f(const uint4& w, float* f) {
   }
 }
 
-__device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+// 16-byte asynchronous copy global -> shared (L2 only): the weight stream is
+// staged through a per-warp ring in shared memory, so the chunks in flight
+// hold no registers.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Ring stages per lane (chunks of the four weight rows in flight); fewer when
+// four activation rows take most of the shared memory.
+template <int MR>
+constexpr int ring_stages() { return MR >= 4 ? 2 : 4; }
+constexpr size_t ring_bytes(int stages) { return (size_t)kDecWarps * stages * kRowsPerWarp * 32 * 16; }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -77,11 +88,14 @@ __device__ __forceinline__ void unit_range(int total, int& u0, int& u1) {
 // GEMM1 + SwiGLU.  Unit = (tile, 32 intermediate columns j); warp w takes
 // columns j0 + 2w and j0 + 2w + 1 (their gate rows j and up rows j + I).
 template <int MR>
-__global__ void __launch_bounds__(kDecThreads) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter) {
+__global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter) {
   extern __shared__ float smem[];
   const int H = a.H, I = a.I, KB = H / kBlock, NC = H / kChunk;
   float* sA = smem;                        // [MR][16][NC]
   float* sS = smem + (size_t)MR * H;       // [MR][KB] activation scales
+  constexpr int S = ring_stages<MR>();
+  uint4* ring = reinterpret_cast<uint4*>(smem + (((size_t)MR * (H + KB) + 3) & ~(size_t)3)) +
+                (size_t)(threadIdx.x >> 5) * S * kRowsPerWarp * 32;  // this warp's [S][4][32] chunks
   const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
   const int per_tile = I / (2 * kDecWarps);
   int u0, u1;
@@ -127,18 +141,30 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm1_kernel(Gemm1Args a, 
     for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
       for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
-    // two chunks of loads in flight per lane: the next chunk's weights are
-    // requested before this chunk's arithmetic
-    uint4 wv[kRowsPerWarp], wn[kRowsPerWarp];
-    if (lane < NC) {
+    // S - 1 chunks of the four rows in flight per lane through the ring
+    const int n_it = (NC - lane + 31) / 32;  // chunks c = lane + 32 * it
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ldg_stream(wrow[q] + (size_t)lane * kChunk);
-    }
-    for (int c = lane; c < NC; c += 32) {
-      if (c + 32 < NC) {
+    for (int st = 0; st < S - 1; ++st) {
+      if (st < n_it) {
 #pragma unroll
-        for (int q = 0; q < kRowsPerWarp; ++q) wn[q] = ldg_stream(wrow[q] + (size_t)(c + 32) * kChunk);
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          cp_async16(ring + (st * kRowsPerWarp + q) * 32 + lane, wrow[q] + (size_t)(lane + 32 * st) * kChunk);
       }
+      cp_async_commit();
+    }
+    for (int it = 0; it < n_it; ++it) {
+      const int nx = it + S - 1;
+      if (nx < n_it) {
+#pragma unroll
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          cp_async16(ring + ((nx % S) * kRowsPerWarp + q) * 32 + lane, wrow[q] + (size_t)(lane + 32 * nx) * kChunk);
+      }
+      cp_async_commit();
+      cp_async_wait<S - 1>();  // chunk it has landed
+      uint4 wv[kRowsPerWarp];
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((it % S) * kRowsPerWarp + q) * 32 + lane];
+      const int c = lane + 32 * it;
       const int kb = c / (kBlock / kChunk);
       float part[kRowsPerWarp][MR];
 #pragma unroll
@@ -160,9 +186,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm1_kernel(Gemm1Args a, 
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[q][r], sS[r * KB + kb] * ws, acc[q][r]);
       }
-#pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = wn[q];
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
@@ -184,10 +209,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm1_kernel(Gemm1Args a, 
 // GEMM2 + routing weight.  Unit = (tile, 64 output columns h); warp w takes
 // h0 + 4w .. h0 + 4w + 3.
 template <int MR>
-__global__ void __launch_bounds__(kDecThreads) decode_gemm2_kernel(Gemm2Args a, const float* __restrict__ inter) {
+__global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args a, const float* __restrict__ inter) {
   extern __shared__ float smem[];
   const int H = a.H, I = a.I, KB = I / kBlock, NC = I / kChunk;
   float* sC = smem;  // [MR][16][NC]
+  constexpr int S = 4;
+  uint4* ring = reinterpret_cast<uint4*>(smem + (size_t)MR * I) + (size_t)(threadIdx.x >> 5) * S * kRowsPerWarp * 32;
   const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
   const int per_tile = H / (kRowsPerWarp * kDecWarps);
   int u0, u1;
@@ -216,17 +243,31 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm2_kernel(Gemm2Args a, 
     for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
       for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
-    uint4 wv[kRowsPerWarp], wn[kRowsPerWarp];
-    if (lane < NC) {
+    const int n_it = (NC - lane + 31) / 32;
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ldg_stream(W + (size_t)(h0 + q) * I + (size_t)lane * kChunk);
-    }
-    for (int c = lane; c < NC; c += 32) {
-      if (c + 32 < NC) {
+    for (int st = 0; st < S - 1; ++st) {
+      if (st < n_it) {
 #pragma unroll
         for (int q = 0; q < kRowsPerWarp; ++q)
-          wn[q] = ldg_stream(W + (size_t)(h0 + q) * I + (size_t)(c + 32) * kChunk);
+          cp_async16(ring + (st * kRowsPerWarp + q) * 32 + lane,
+                     W + (size_t)(h0 + q) * I + (size_t)(lane + 32 * st) * kChunk);
       }
+      cp_async_commit();
+    }
+    for (int it = 0; it < n_it; ++it) {
+      const int nx = it + S - 1;
+      if (nx < n_it) {
+#pragma unroll
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          cp_async16(ring + ((nx % S) * kRowsPerWarp + q) * 32 + lane,
+                     W + (size_t)(h0 + q) * I + (size_t)(lane + 32 * nx) * kChunk);
+      }
+      cp_async_commit();
+      cp_async_wait<S - 1>();
+      uint4 wv[kRowsPerWarp];
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((it % S) * kRowsPerWarp + q) * 32 + lane];
+      const int c = lane + 32 * it;
       const int kb = c / (kBlock / kChunk);
 #pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
@@ -243,9 +284,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm2_kernel(Gemm2Args a, 
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[r], ws, acc[q][r]);
       }
-#pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = wn[q];
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
@@ -272,7 +312,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_gemm2_kernel(Gemm2Args a, 
 
 // Dynamic shared memory above 48 KB needs a per-device opt-in per kernel; the
 // bound is the largest size shape_ok admits.
-constexpr int kDecSmemMax = 200 * 1024;
+constexpr int kDecSmemMax = 227 * 1024;
 
 template <class K>
 int allow_smem(K kernel, std::atomic<uint32_t>& done) {
@@ -289,11 +329,12 @@ int allow_smem(K kernel, std::atomic<uint32_t>& done) {
 template <int MR>
 int launch_gemm1_mr(const Gemm1Args& g1, float* inter, cudaStream_t s) {
   static std::atomic<uint32_t> done{0};
-  const size_t smem = sizeof(float) * ((size_t)MR * g1.H + (size_t)MR * (g1.H / kBlock));
+  const size_t smem = ((sizeof(float) * ((size_t)MR * g1.H + (size_t)MR * (g1.H / kBlock)) + 15) & ~(size_t)15) +
+                      ring_bytes(ring_stages<MR>());
   int rc;
   if ((rc = allow_smem(decode_gemm1_kernel<MR>, done))) return rc;
-  // one CTA of 16 warps per SM (its registers fill the SM's file), each
-  // keeping two chunks of four weight rows in flight per lane
+  // one CTA of 16 warps per SM, each lane keeping S - 1 chunks of four weight
+  // rows in flight through its ring
   decode_gemm1_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g1, inter);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
@@ -302,7 +343,7 @@ int launch_gemm1_mr(const Gemm1Args& g1, float* inter, cudaStream_t s) {
 template <int MR>
 int launch_gemm2_mr(const Gemm2Args& g2, const float* inter, cudaStream_t s) {
   static std::atomic<uint32_t> done{0};
-  const size_t smem = sizeof(float) * (size_t)MR * g2.I;
+  const size_t smem = sizeof(float) * (size_t)MR * g2.I + ring_bytes(4);
   int rc;
   if ((rc = allow_smem(decode_gemm2_kernel<MR>, done))) return rc;
   decode_gemm2_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g2, inter);
@@ -312,8 +353,10 @@ int launch_gemm2_mr(const Gemm2Args& g2, const float* inter, cudaStream_t s) {
 
 int shape_ok(int H, int I) {
   return H % (kRowsPerWarp * kDecWarps) == 0 && I % (2 * kDecWarps) == 0 && H % kBlock == 0 && I % kBlock == 0 &&
-         (size_t)kDecodeMaxRows * (H + H / kBlock) * sizeof(float) <= (size_t)kDecSmemMax &&
-         (size_t)kDecodeMaxRows * I * sizeof(float) <= (size_t)kDecSmemMax;
+         (size_t)kDecodeMaxRows * (H + H / kBlock) * sizeof(float) + 16 + ring_bytes(ring_stages<kDecodeMaxRows>()) <=
+             (size_t)kDecSmemMax &&
+         (size_t)2 * (H + H / kBlock) * sizeof(float) + 16 + ring_bytes(ring_stages<2>()) <= (size_t)kDecSmemMax &&
+         (size_t)kDecodeMaxRows * I * sizeof(float) + ring_bytes(4) <= (size_t)kDecSmemMax;
 }
 
 }  // namespace
