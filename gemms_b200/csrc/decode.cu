@@ -92,6 +92,34 @@ __device__ __forceinline__ void unit_range(int total, int& u0, int& u1) {
 // has the same item count (chunks past the row end are skipped), so the
 // block-wide barriers of a tile change line up.
 
+// Tile metadata (group, first row, rows) of the CTA's units, read once into
+// shared memory so that neither side of the stream waits on global loads at a
+// unit switch.  Units past kMetaUnits (never at T <= 4) read it directly.
+constexpr int kMetaUnits = 64;
+
+struct TileMeta {
+  int g, row0, rows;
+};
+
+template <int MR>
+__device__ __forceinline__ void load_meta(const GemmGroupsArgs& gg, int u0, int u1, int per_tile, int* s_meta) {
+  for (int i = threadIdx.x; i < min(u1 - u0, kMetaUnits); i += blockDim.x) {
+    const int tile = (u0 + i) / per_tile;
+    s_meta[3 * i] = gg.tile_group[tile];
+    s_meta[3 * i + 1] = gg.tile_row0[tile];
+    s_meta[3 * i + 2] = min(gg.tile_rows[tile], MR);
+  }
+}
+
+template <int MR>
+__device__ __forceinline__ TileMeta unit_meta(const GemmGroupsArgs& gg, int u, int u0, int per_tile,
+                                              const int* s_meta) {
+  const int i = u - u0;
+  if (i < kMetaUnits) return TileMeta{s_meta[3 * i], s_meta[3 * i + 1], s_meta[3 * i + 2]};
+  const int tile = u / per_tile;
+  return TileMeta{gg.tile_group[tile], gg.tile_row0[tile], min(gg.tile_rows[tile], MR)};
+}
+
 // Weight rows and scale rows of GEMM1 unit u for warp w: gate j0, j0+1, up
 // j0, j0+1 (j0 = 32 * (u % per_tile) + 2w).
 struct G1Unit {
@@ -101,14 +129,16 @@ struct G1Unit {
 };
 
 template <int MR>
-__device__ __forceinline__ G1Unit g1_unit(const Gemm1Args& a, int u, int per_tile, int warp) {
+__device__ __forceinline__ G1Unit g1_unit(const Gemm1Args& a, int u, int u0, int per_tile, int warp,
+                                          const int* s_meta) {
   G1Unit r;
   const int H = a.H, I = a.I, KB = H / kBlock;
   r.tile = u / per_tile;
   const int jc = u - r.tile * per_tile;
-  const int g = a.g.tile_group[r.tile];
-  r.row0 = a.g.tile_row0[r.tile];
-  r.rows = min(a.g.tile_rows[r.tile], MR);
+  const TileMeta m = unit_meta<MR>(a.g, u, u0, per_tile, s_meta);
+  const int g = m.g;
+  r.row0 = m.row0;
+  r.rows = m.rows;
   const bool sh = g == a.g.shared_group;
   const uint8_t* W = sh ? a.sw13 : a.w13 + (size_t)g * 2 * I * H;
   const float* WS = sh ? a.sw13_scale : a.w13_scale + (size_t)g * (2 * I / kBlock) * KB;
@@ -138,17 +168,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
   const int per_tile = I / (2 * kDecWarps);
   int u0, u1;
   unit_range(num_tiles * per_tile, u0, u1);
+  __shared__ int s_meta[3 * kMetaUnits];
+  load_meta<MR>(a.g, u0, u1, per_tile, s_meta);
+  __syncthreads();
   const int n_it = (NC + 31) / 32;
   const int n_items = (u1 - u0) * n_it;
   // request item k (chunk lane + 32 * (k % n_it) of unit u0 + k / n_it) into ring slot k % S
+  // the issuing side runs S - 1 items ahead; its unit record is recomputed
+  // only when it crosses into the next unit (tile metadata loads once per unit)
+  int iss_u = -1;
+  G1Unit iss{};
   auto issue = [&](int k) {
     if (k < n_items) {
       const int it = k % n_it, c = lane + 32 * it;
+      const int u = u0 + k / n_it;
+      if (u != iss_u) {
+        iss = g1_unit<MR>(a, u, u0, per_tile, warp, s_meta);
+        iss_u = u;
+      }
       if (c < NC) {
-        const G1Unit w = g1_unit<MR>(a, u0 + k / n_it, per_tile, warp);
 #pragma unroll
         for (int q = 0; q < kRowsPerWarp; ++q)
-          cp_async16(ring + ((k % S) * kRowsPerWarp + q) * 32 + lane, w.row[q] + (size_t)c * kChunk);
+          cp_async16(ring + ((k % S) * kRowsPerWarp + q) * 32 + lane, iss.row[q] + (size_t)c * kChunk);
       }
     }
     cp_async_commit();
@@ -161,7 +202,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
   for (int k = 0; k < n_items; ++k) {
     const int it = k % n_it;
     if (it == 0) {  // a unit starts
-      cur = g1_unit<MR>(a, u0 + k / n_it, per_tile, warp);
+      cur = g1_unit<MR>(a, u0 + k / n_it, u0, per_tile, warp, s_meta);
       if (cur.tile != staged) {
         __syncthreads();  // the previous tile's rows are no longer read
         for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
@@ -246,14 +287,16 @@ struct G2Unit {
 };
 
 template <int MR>
-__device__ __forceinline__ G2Unit g2_unit(const Gemm2Args& a, int u, int per_tile, int warp) {
+__device__ __forceinline__ G2Unit g2_unit(const Gemm2Args& a, int u, int u0, int per_tile, int warp,
+                                          const int* s_meta) {
   G2Unit r;
   const int H = a.H, I = a.I, KB = I / kBlock;
   r.tile = u / per_tile;
   const int hc = u - r.tile * per_tile;
-  const int g = a.g.tile_group[r.tile];
-  r.row0 = a.g.tile_row0[r.tile];
-  r.rows = min(a.g.tile_rows[r.tile], MR);
+  const TileMeta m = unit_meta<MR>(a.g, u, u0, per_tile, s_meta);
+  const int g = m.g;
+  r.row0 = m.row0;
+  r.rows = m.rows;
   const bool sh = g == a.g.shared_group;
   r.W = sh ? a.sw2 : a.w2 + (size_t)g * H * I;
   r.WS = sh ? a.sw2_scale : a.w2_scale + (size_t)g * (H / kBlock) * KB;
@@ -275,17 +318,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
   const int per_tile = H / (kRowsPerWarp * kDecWarps);
   int u0, u1;
   unit_range(num_tiles * per_tile, u0, u1);
+  __shared__ int s_meta[3 * kMetaUnits];
+  load_meta<MR>(a.g, u0, u1, per_tile, s_meta);
+  __syncthreads();
   const int n_it = (NC + 31) / 32;
   const int n_items = (u1 - u0) * n_it;
+  int iss_u = -1;
+  G2Unit iss{};
   auto issue = [&](int k) {
     if (k < n_items) {
       const int it = k % n_it, c = lane + 32 * it;
+      const int u = u0 + k / n_it;
+      if (u != iss_u) {
+        iss = g2_unit<MR>(a, u, u0, per_tile, warp, s_meta);
+        iss_u = u;
+      }
       if (c < NC) {
-        const G2Unit w = g2_unit<MR>(a, u0 + k / n_it, per_tile, warp);
 #pragma unroll
         for (int q = 0; q < kRowsPerWarp; ++q)
           cp_async16(ring + ((k % S) * kRowsPerWarp + q) * 32 + lane,
-                     w.W + (size_t)(w.h0 + q) * I + (size_t)c * kChunk);
+                     iss.W + (size_t)(iss.h0 + q) * I + (size_t)c * kChunk);
       }
     }
     cp_async_commit();
@@ -298,7 +350,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
   for (int k = 0; k < n_items; ++k) {
     const int it = k % n_it;
     if (it == 0) {
-      cur = g2_unit<MR>(a, u0 + k / n_it, per_tile, warp);
+      cur = g2_unit<MR>(a, u0 + k / n_it, u0, per_tile, warp, s_meta);
       if (cur.tile != staged) {
         __syncthreads();
         for (int i = threadIdx.x; i < MR * I; i += blockDim.x) {
@@ -367,7 +419,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
 
 // Dynamic shared memory above 48 KB needs a per-device opt-in per kernel; the
 // bound is the largest size shape_ok admits.
-constexpr int kDecSmemMax = 227 * 1024;
+constexpr int kDecSmemMax = 225 * 1024;  // + static shared memory (unit metadata) <= 227 KB opt-in
 
 template <class K>
 int allow_smem(K kernel, std::atomic<uint32_t>& done) {

@@ -34,6 +34,21 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi)
   }
 }
 
+// pp[0] + pp[stride] + ... + pp[(n-1)*stride], added in index order; the loads
+// are issued eight at a time (independent), only the additions are chained.
+__device__ __forceinline__ float sum_partials_in_order(const float* pp, int n, size_t stride) {
+  float x = 0.f;
+  for (int q0 = 0; q0 < n; q0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = q0 + q < n ? pp[(size_t)(q0 + q) * stride] : 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q0 + q < n) x = (q0 + q == 0) ? v[q] : __fadd_rn(x, v[q]);
+  }
+  return x;
+}
+
 // One warp per token.  Lane l holds experts e = j*32 + l (j < V).
 // Sigmoid: exp is evaluated in double and rounded to fp32 (correctly rounded
 // in practice), then 1/(1+e) and + bias in IEEE fp32 -- the oracle computes
@@ -56,9 +71,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       float x;
       if (a.partials) {
         // router-GEMM split-K partials, summed in split order (deterministic)
-        const float* pp = a.partials + (size_t)t * E + e;
-        x = pp[0];
-        for (int q = 1; q < a.n_partials; ++q) x = __fadd_rn(x, pp[(size_t)q * a.T * E]);
+        x = sum_partials_in_order(a.partials + (size_t)t * E + e, a.n_partials, (size_t)a.T * E);
         if (a.logits_out) a.logits_out[(size_t)t * E + e] = x;
       } else {
         x = __ldg(a.logits + (size_t)t * E + e);
@@ -190,9 +203,7 @@ __global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
   if (live) {
     float x;
     if (a.partials) {
-      const float* pp = a.partials + (size_t)t * E + e;
-      x = pp[0];
-      for (int q = 1; q < a.n_partials; ++q) x = __fadd_rn(x, pp[(size_t)q * a.T * E]);
+      x = sum_partials_in_order(a.partials + (size_t)t * E + e, a.n_partials, (size_t)a.T * E);
       if (a.logits_out) a.logits_out[(size_t)t * E + e] = x;
     } else {
       x = __ldg(a.logits + (size_t)t * E + e);
@@ -473,7 +484,9 @@ int launch_plan(const PlanArgs& a, cudaStream_t s) {
 int launch_assign(const AssignArgs& a, cudaStream_t s) {
   const int blocks = a.E_local + (a.shared_rows > 0 ? 1 : 0);
   if (blocks == 0 || a.T <= 0) return GEMMS_OK;
-  assign_kernel<<<blocks, 1024, 0, s>>>(a);
+  // few tokens: a block as wide as the tokens (whole warps), not 1024 idle threads
+  const int threads = a.T_dev ? 1024 : std::min(1024, std::max(32, (a.T + 31) / 32 * 32));
+  assign_kernel<<<blocks, threads, 0, s>>>(a);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }
