@@ -85,75 +85,8 @@ __device__ __forceinline__ void unit_range(int total, int& u0, int& u1) {
   u1 = min(total, u0 + per);
 }
 
-// Both kernels run each lane through one flat stream of items (unit, chunk)
-// over the CTA's whole unit range, so the ring keeps S - 1 chunks in flight
-// across unit boundaries: the next unit's weights are requested while the
-// current unit's last chunks are multiplied and its sums reduced.  Every lane
-// has the same item count (chunks past the row end are skipped), so the
-// block-wide barriers of a tile change line up.
-
-// Tile metadata (group, first row, rows) of the CTA's units, read once into
-// shared memory so that neither side of the stream waits on global loads at a
-// unit switch.  Units past kMetaUnits (never at T <= 4) read it directly.
-constexpr int kMetaUnits = 64;
-
-struct TileMeta {
-  int g, row0, rows;
-};
-
-template <int MR>
-__device__ __forceinline__ void load_meta(const GemmGroupsArgs& gg, int u0, int u1, int per_tile, int* s_meta) {
-  for (int i = threadIdx.x; i < min(u1 - u0, kMetaUnits); i += blockDim.x) {
-    const int tile = (u0 + i) / per_tile;
-    s_meta[3 * i] = gg.tile_group[tile];
-    s_meta[3 * i + 1] = gg.tile_row0[tile];
-    s_meta[3 * i + 2] = min(gg.tile_rows[tile], MR);
-  }
-}
-
-template <int MR>
-__device__ __forceinline__ TileMeta unit_meta(const GemmGroupsArgs& gg, int u, int u0, int per_tile,
-                                              const int* s_meta) {
-  const int i = u - u0;
-  if (i < kMetaUnits) return TileMeta{s_meta[3 * i], s_meta[3 * i + 1], s_meta[3 * i + 2]};
-  const int tile = u / per_tile;
-  return TileMeta{gg.tile_group[tile], gg.tile_row0[tile], min(gg.tile_rows[tile], MR)};
-}
-
-// Weight rows and scale rows of GEMM1 unit u for warp w: gate j0, j0+1, up
-// j0, j0+1 (j0 = 32 * (u % per_tile) + 2w).
-struct G1Unit {
-  const uint8_t* row[kRowsPerWarp];
-  const float* sc[kRowsPerWarp];
-  int tile, row0, rows, j0;
-};
-
-template <int MR>
-__device__ __forceinline__ G1Unit g1_unit(const Gemm1Args& a, int u, int u0, int per_tile, int warp,
-                                          const int* s_meta) {
-  G1Unit r;
-  const int H = a.H, I = a.I, KB = H / kBlock;
-  r.tile = u / per_tile;
-  const int jc = u - r.tile * per_tile;
-  const TileMeta m = unit_meta<MR>(a.g, u, u0, per_tile, s_meta);
-  const int g = m.g;
-  r.row0 = m.row0;
-  r.rows = m.rows;
-  const bool sh = g == a.g.shared_group;
-  const uint8_t* W = sh ? a.sw13 : a.w13 + (size_t)g * 2 * I * H;
-  const float* WS = sh ? a.sw13_scale : a.w13_scale + (size_t)g * (2 * I / kBlock) * KB;
-  r.j0 = jc * 2 * kDecWarps + 2 * warp;
-  const int rows_n[kRowsPerWarp] = {r.j0, r.j0 + 1, I + r.j0, I + r.j0 + 1};
-#pragma unroll
-  for (int q = 0; q < kRowsPerWarp; ++q) {
-    r.row[q] = W + (size_t)rows_n[q] * H;
-    r.sc[q] = WS + (size_t)(rows_n[q] / kBlock) * KB;
-  }
-  return r;
-}
-
 // GEMM1 + SwiGLU.  Unit = (tile, 32 intermediate columns j); warp w takes
-// columns j0 and j0 + 1 (their gate rows j and up rows j + I).
+// columns j0 + 2w and j0 + 2w + 1 (their gate rows j and up rows j + I).
 template <int MR>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter) {
   extern __shared__ float smem[];
@@ -161,81 +94,77 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
   float* sA = smem;                        // [MR][16][NC]
   float* sS = smem + (size_t)MR * H;       // [MR][KB] activation scales
   constexpr int S = ring_stages<MR>();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint4* ring = reinterpret_cast<uint4*>(smem + (((size_t)MR * (H + KB) + 3) & ~(size_t)3)) +
-                (size_t)warp * S * kRowsPerWarp * 32;  // this warp's [S][4][32] chunks
+                (size_t)(threadIdx.x >> 5) * S * kRowsPerWarp * 32;  // this warp's [S][4][32] chunks
   const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
   const int per_tile = I / (2 * kDecWarps);
   int u0, u1;
   unit_range(num_tiles * per_tile, u0, u1);
-  __shared__ int s_meta[3 * kMetaUnits];
-  load_meta<MR>(a.g, u0, u1, per_tile, s_meta);
-  __syncthreads();
-  const int n_it = (NC + 31) / 32;
-  const int n_items = (u1 - u0) * n_it;
-  // request item k (chunk lane + 32 * (k % n_it) of unit u0 + k / n_it) into ring slot k % S
-  // the issuing side runs S - 1 items ahead; its unit record is recomputed
-  // only when it crosses into the next unit (tile metadata loads once per unit)
-  int iss_u = -1;
-  G1Unit iss{};
-  auto issue = [&](int k) {
-    if (k < n_items) {
-      const int it = k % n_it, c = lane + 32 * it;
-      const int u = u0 + k / n_it;
-      if (u != iss_u) {
-        iss = g1_unit<MR>(a, u, u0, per_tile, warp, s_meta);
-        iss_u = u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int staged = -1;
+  for (int u = u0; u < u1; ++u) {
+    const int tile = u / per_tile, jc = u - tile * per_tile;
+    const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
+    if (tile != staged) {
+      __syncthreads();  // previous tile's rows no longer read
+      for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
+        const int r = i / NC, c = i - r * NC;
+        float f[kChunk];
+        if (r < rows) {
+          e4m3x16_to_f(*reinterpret_cast<const uint4*>(a.a + (size_t)(row0 + r) * H + (size_t)c * kChunk), f);
+        } else {
+#pragma unroll
+          for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
       }
-      if (c < NC) {
+      for (int i = threadIdx.x; i < MR * KB; i += blockDim.x) {
+        const int r = i / KB, kb = i - r * KB;
+        sS[i] = r < rows ? a.a_scale[(size_t)kb * a.a_scale_ld + row0 + r] : 0.f;
+      }
+      __syncthreads();
+      staged = tile;
+    }
+    const bool sh = g == a.g.shared_group;
+    const uint8_t* W = sh ? a.sw13 : a.w13 + (size_t)g * 2 * I * H;
+    const float* WS = sh ? a.sw13_scale : a.w13_scale + (size_t)g * (2 * I / kBlock) * KB;
+    const int j0 = jc * 2 * kDecWarps + 2 * warp;
+    // weight rows: gate j0, gate j0+1, up j0, up j0+1
+    const uint8_t* wrow[kRowsPerWarp] = {W + (size_t)j0 * H, W + (size_t)(j0 + 1) * H, W + (size_t)(I + j0) * H,
+                                         W + (size_t)(I + j0 + 1) * H};
+    const float* wsc[kRowsPerWarp] = {WS + (size_t)(j0 / kBlock) * KB, WS + (size_t)((j0 + 1) / kBlock) * KB,
+                                      WS + (size_t)((I + j0) / kBlock) * KB,
+                                      WS + (size_t)((I + j0 + 1) / kBlock) * KB};
+    float acc[kRowsPerWarp][MR];
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
+    // S - 1 chunks of the four rows in flight per lane through the ring
+    const int n_it = (NC - lane + 31) / 32;  // chunks c = lane + 32 * it
+#pragma unroll
+    for (int st = 0; st < S - 1; ++st) {
+      if (st < n_it) {
 #pragma unroll
         for (int q = 0; q < kRowsPerWarp; ++q)
-          cp_async16(ring + ((k % S) * kRowsPerWarp + q) * 32 + lane, iss.row[q] + (size_t)c * kChunk);
+          cp_async16(ring + (st * kRowsPerWarp + q) * 32 + lane, wrow[q] + (size_t)(lane + 32 * st) * kChunk);
       }
+      cp_async_commit();
     }
-    cp_async_commit();
-  };
+    for (int it = 0; it < n_it; ++it) {
+      const int nx = it + S - 1;
+      if (nx < n_it) {
 #pragma unroll
-  for (int k = 0; k < S - 1; ++k) issue(k);
-  int staged = -1;
-  G1Unit cur{};
-  float acc[kRowsPerWarp][MR];
-  for (int k = 0; k < n_items; ++k) {
-    const int it = k % n_it;
-    if (it == 0) {  // a unit starts
-      cur = g1_unit<MR>(a, u0 + k / n_it, u0, per_tile, warp, s_meta);
-      if (cur.tile != staged) {
-        __syncthreads();  // the previous tile's rows are no longer read
-        for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
-          const int r = i / NC, c = i - r * NC;
-          float f[kChunk];
-          if (r < cur.rows) {
-            e4m3x16_to_f(*reinterpret_cast<const uint4*>(a.a + (size_t)(cur.row0 + r) * H + (size_t)c * kChunk), f);
-          } else {
-#pragma unroll
-            for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
-          }
-#pragma unroll
-          for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
-        }
-        for (int i = threadIdx.x; i < MR * KB; i += blockDim.x) {
-          const int r = i / KB, kb = i - r * KB;
-          sS[i] = r < cur.rows ? a.a_scale[(size_t)kb * a.a_scale_ld + cur.row0 + r] : 0.f;
-        }
-        __syncthreads();
-        staged = cur.tile;
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          cp_async16(ring + ((nx % S) * kRowsPerWarp + q) * 32 + lane, wrow[q] + (size_t)(lane + 32 * nx) * kChunk);
       }
-#pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q)
-#pragma unroll
-        for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
-    }
-    issue(k + S - 1);
-    cp_async_wait<S - 1>();  // item k has landed
-    const int c = lane + 32 * it;
-    if (c < NC) {
+      cp_async_commit();
+      cp_async_wait<S - 1>();  // chunk it has landed
       uint4 wv[kRowsPerWarp];
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((k % S) * kRowsPerWarp + q) * 32 + lane];
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((it % S) * kRowsPerWarp + q) * 32 + lane];
+      const int c = lane + 32 * it;
       const int kb = c / (kBlock / kChunk);
       float part[kRowsPerWarp][MR];
 #pragma unroll
@@ -253,126 +182,92 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
       }
 #pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
-        const float ws = __ldg(cur.sc[q] + kb);
+        const float ws = __ldg(wsc[q] + kb);
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[q][r], sS[r * KB + kb] * ws, acc[q][r]);
       }
     }
-    if (it == n_it - 1) {  // the unit's last chunk: reduce and write
+    cp_async_wait<0>();
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q)
+    for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
-        for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
-      if (lane < 2 * MR) {  // lane = (column j0 + (lane & 1), row lane >> 1)
-        const int jj = lane & 1, r = lane >> 1;
-        float gate = 0.f, up = 0.f;
+      for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
+    if (lane < 2 * MR) {  // lane = (column j0 + (lane & 1), row lane >> 1)
+      const int jj = lane & 1, r = lane >> 1;
+      float gate = 0.f, up = 0.f;
 #pragma unroll
-        for (int rr = 0; rr < MR; ++rr)
-          if (rr == r) {
-            gate = jj ? acc[1][rr] : acc[0][rr];
-            up = jj ? acc[3][rr] : acc[2][rr];
-          }
-        if (r < cur.rows)
-          inter[(size_t)(cur.row0 + r) * I + cur.j0 + jj] = up * sm100::rcp_approx(1.0f + __expf(-up)) * gate;
-      }
+      for (int rr = 0; rr < MR; ++rr)
+        if (rr == r) {
+          gate = jj ? acc[1][rr] : acc[0][rr];
+          up = jj ? acc[3][rr] : acc[2][rr];
+        }
+      if (r < rows) inter[(size_t)(row0 + r) * I + j0 + jj] = up * sm100::rcp_approx(1.0f + __expf(-up)) * gate;
     }
   }
-  cp_async_wait<0>();
-}
-
-struct G2Unit {
-  const uint8_t* W;
-  const float* WS;
-  int tile, row0, rows, h0;
-};
-
-template <int MR>
-__device__ __forceinline__ G2Unit g2_unit(const Gemm2Args& a, int u, int u0, int per_tile, int warp,
-                                          const int* s_meta) {
-  G2Unit r;
-  const int H = a.H, I = a.I, KB = I / kBlock;
-  r.tile = u / per_tile;
-  const int hc = u - r.tile * per_tile;
-  const TileMeta m = unit_meta<MR>(a.g, u, u0, per_tile, s_meta);
-  const int g = m.g;
-  r.row0 = m.row0;
-  r.rows = m.rows;
-  const bool sh = g == a.g.shared_group;
-  r.W = sh ? a.sw2 : a.w2 + (size_t)g * H * I;
-  r.WS = sh ? a.sw2_scale : a.w2_scale + (size_t)g * (H / kBlock) * KB;
-  r.h0 = hc * kRowsPerWarp * kDecWarps + kRowsPerWarp * warp;
-  return r;
 }
 
 // GEMM2 + routing weight.  Unit = (tile, 64 output columns h); warp w takes
-// h0 .. h0 + 3.
+// h0 + 4w .. h0 + 4w + 3.
 template <int MR>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args a, const float* __restrict__ inter) {
   extern __shared__ float smem[];
   const int H = a.H, I = a.I, KB = I / kBlock, NC = I / kChunk;
   float* sC = smem;  // [MR][16][NC]
   constexpr int S = 4;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint4* ring = reinterpret_cast<uint4*>(smem + (size_t)MR * I) + (size_t)warp * S * kRowsPerWarp * 32;
+  uint4* ring = reinterpret_cast<uint4*>(smem + (size_t)MR * I) + (size_t)(threadIdx.x >> 5) * S * kRowsPerWarp * 32;
   const int num_tiles = min(*a.g.num_tiles, a.g.max_tiles);
   const int per_tile = H / (kRowsPerWarp * kDecWarps);
   int u0, u1;
   unit_range(num_tiles * per_tile, u0, u1);
-  __shared__ int s_meta[3 * kMetaUnits];
-  load_meta<MR>(a.g, u0, u1, per_tile, s_meta);
-  __syncthreads();
-  const int n_it = (NC + 31) / 32;
-  const int n_items = (u1 - u0) * n_it;
-  int iss_u = -1;
-  G2Unit iss{};
-  auto issue = [&](int k) {
-    if (k < n_items) {
-      const int it = k % n_it, c = lane + 32 * it;
-      const int u = u0 + k / n_it;
-      if (u != iss_u) {
-        iss = g2_unit<MR>(a, u, u0, per_tile, warp, s_meta);
-        iss_u = u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int staged = -1;
+  for (int u = u0; u < u1; ++u) {
+    const int tile = u / per_tile, hc = u - tile * per_tile;
+    const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
+    if (tile != staged) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < MR * I; i += blockDim.x) {
+        const int r = i / I, k = i - r * I;  // consecutive threads: consecutive k (coalesced global reads)
+        const int c = k / kChunk, e = k - c * kChunk;
+        sC[((size_t)r * kChunk + e) * NC + c] = r < rows ? inter[(size_t)(row0 + r) * I + k] : 0.f;
       }
-      if (c < NC) {
+      __syncthreads();
+      staged = tile;
+    }
+    const bool sh = g == a.g.shared_group;
+    const uint8_t* W = sh ? a.sw2 : a.w2 + (size_t)g * H * I;
+    const float* WS = sh ? a.sw2_scale : a.w2_scale + (size_t)g * (H / kBlock) * KB;
+    const int h0 = hc * kRowsPerWarp * kDecWarps + kRowsPerWarp * warp;
+    float acc[kRowsPerWarp][MR];
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
+    const int n_it = (NC - lane + 31) / 32;
+#pragma unroll
+    for (int st = 0; st < S - 1; ++st) {
+      if (st < n_it) {
 #pragma unroll
         for (int q = 0; q < kRowsPerWarp; ++q)
-          cp_async16(ring + ((k % S) * kRowsPerWarp + q) * 32 + lane,
-                     iss.W + (size_t)(iss.h0 + q) * I + (size_t)c * kChunk);
+          cp_async16(ring + (st * kRowsPerWarp + q) * 32 + lane,
+                     W + (size_t)(h0 + q) * I + (size_t)(lane + 32 * st) * kChunk);
       }
+      cp_async_commit();
     }
-    cp_async_commit();
-  };
+    for (int it = 0; it < n_it; ++it) {
+      const int nx = it + S - 1;
+      if (nx < n_it) {
 #pragma unroll
-  for (int k = 0; k < S - 1; ++k) issue(k);
-  int staged = -1;
-  G2Unit cur{};
-  float acc[kRowsPerWarp][MR];
-  for (int k = 0; k < n_items; ++k) {
-    const int it = k % n_it;
-    if (it == 0) {
-      cur = g2_unit<MR>(a, u0 + k / n_it, u0, per_tile, warp, s_meta);
-      if (cur.tile != staged) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < MR * I; i += blockDim.x) {
-          const int r = i / I, kk = i - r * I;  // consecutive threads: consecutive columns (coalesced reads)
-          const int c = kk / kChunk, e = kk - c * kChunk;
-          sC[((size_t)r * kChunk + e) * NC + c] = r < cur.rows ? inter[(size_t)(cur.row0 + r) * I + kk] : 0.f;
-        }
-        __syncthreads();
-        staged = cur.tile;
+        for (int q = 0; q < kRowsPerWarp; ++q)
+          cp_async16(ring + ((nx % S) * kRowsPerWarp + q) * 32 + lane,
+                     W + (size_t)(h0 + q) * I + (size_t)(lane + 32 * nx) * kChunk);
       }
-#pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q)
-#pragma unroll
-        for (int r = 0; r < MR; ++r) acc[q][r] = 0.f;
-    }
-    issue(k + S - 1);
-    cp_async_wait<S - 1>();
-    const int c = lane + 32 * it;
-    if (c < NC) {
+      cp_async_commit();
+      cp_async_wait<S - 1>();
       uint4 wv[kRowsPerWarp];
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((k % S) * kRowsPerWarp + q) * 32 + lane];
+      for (int q = 0; q < kRowsPerWarp; ++q) wv[q] = ring[((it % S) * kRowsPerWarp + q) * 32 + lane];
+      const int c = lane + 32 * it;
       const int kb = c / (kBlock / kChunk);
 #pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
@@ -385,41 +280,39 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
         for (int e = 0; e < kChunk; ++e)
 #pragma unroll
           for (int r = 0; r < MR; ++r) part[r] = fmaf(f[e], sC[((size_t)r * kChunk + e) * NC + c], part[r]);
-        const float ws = __ldg(cur.WS + (size_t)((cur.h0 + q) / kBlock) * KB + kb);
+        const float ws = __ldg(WS + (size_t)((h0 + q) / kBlock) * KB + kb);
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[r], ws, acc[q][r]);
       }
     }
-    if (it == n_it - 1) {
+    cp_async_wait<0>();
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q)
+    for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
-        for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
-      if (lane < kRowsPerWarp * MR) {  // lane = (column h0 + (lane % 4), row lane / 4)
-        const int q = lane % kRowsPerWarp, r = lane / kRowsPerWarp;
-        float v = 0.f;
+      for (int r = 0; r < MR; ++r) acc[q][r] = warp_sum(acc[q][r]);
+    if (lane < kRowsPerWarp * MR) {  // lane = (column h0 + (lane % 4), row lane / 4)
+      const int q = lane % kRowsPerWarp, r = lane / kRowsPerWarp;
+      float v = 0.f;
 #pragma unroll
-        for (int qq = 0; qq < kRowsPerWarp; ++qq)
+      for (int qq = 0; qq < kRowsPerWarp; ++qq)
 #pragma unroll
-          for (int rr = 0; rr < MR; ++rr)
-            if (qq == q && rr == r) v = acc[qq][rr];
-        if (r < cur.rows) {
-          const int row = cur.row0 + r;
-          v *= a.row_weight[row];
-          if (a.pair_out)
-            a.pair_out[(size_t)row * H + cur.h0 + q] = v;
-          else
-            atomicAdd(a.out + (size_t)a.row_dest[row] * H + cur.h0 + q, v);
-        }
+        for (int rr = 0; rr < MR; ++rr)
+          if (qq == q && rr == r) v = acc[qq][rr];
+      if (r < rows) {
+        const int row = row0 + r;
+        v *= a.row_weight[row];
+        if (a.pair_out)
+          a.pair_out[(size_t)row * H + h0 + q] = v;
+        else
+          atomicAdd(a.out + (size_t)a.row_dest[row] * H + h0 + q, v);
       }
     }
   }
-  cp_async_wait<0>();
 }
 
 // Dynamic shared memory above 48 KB needs a per-device opt-in per kernel; the
 // bound is the largest size shape_ok admits.
-constexpr int kDecSmemMax = 225 * 1024;  // + static shared memory (unit metadata) <= 227 KB opt-in
+constexpr int kDecSmemMax = 227 * 1024;
 
 template <class K>
 int allow_smem(K kernel, std::atomic<uint32_t>& done) {
