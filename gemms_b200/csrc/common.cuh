@@ -87,6 +87,11 @@ struct AssignArgs {
 };
 int launch_assign(const AssignArgs& a, cudaStream_t s);
 
+// Decode-sized batches (T <= 4): route + plan + assign in one launch, same
+// results as launch_route, launch_plan and launch_assign in sequence.
+bool decode_front_ok(const RouteArgs& ra, const PlanArgs& pa);
+int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, cudaStream_t s);
+
 // Gather (and for bf16 input, quantise per 1x128) activation rows into the
 // expert-grouped operand: rows_fp8 [R, H], rows_scale [H/128, ld].
 struct PermuteArgs {

@@ -225,7 +225,6 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   ra.topk_w = at<float>(ws, L.topk_w);
   ra.counts = at<int32_t>(ws, L.counts);
   ra.pair_row = at<int32_t>(ws, L.pair_row);
-  if ((rc = launch_route(ra, st))) return rc;
 
   PlanArgs pa{};
   pa.counts = at<int32_t>(ws, L.counts);
@@ -240,7 +239,6 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   pa.max_tiles = L.max_tiles;
   pa.row_capacity = L.R_max;
   pa.err = err;
-  if ((rc = launch_plan(pa, st))) return rc;
 
   AssignArgs sa{};
   sa.topk_idx = ra.topk_idx;
@@ -255,7 +253,13 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   sa.pair_row = ra.pair_row;
   sa.shared_rows = pa.shared_rows;
   sa.row_capacity = L.R_max;
-  if ((rc = launch_assign(sa, st))) return rc;
+  if (L.decode_rows && decode_front_ok(ra, pa)) {
+    if ((rc = launch_decode_front(ra, pa, sa, st))) return rc;
+  } else {
+    if ((rc = launch_route(ra, st))) return rc;
+    if ((rc = launch_plan(pa, st))) return rc;
+    if ((rc = launch_assign(sa, st))) return rc;
+  }
 
   PermuteArgs qa{};
   qa.mode = s.input_mode;

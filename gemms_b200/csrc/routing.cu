@@ -187,18 +187,29 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
 // top-k under a strict order lies in the union of the warps' top-k).
 constexpr int kRouteBlockMaxT = 64;
 
-__global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
-  __shared__ float s_g[256];           // group scores (n_group <= E / 2)
-  __shared__ int s_kept[256];
-  __shared__ float s_v[8][16], s_s[8][16];
-  __shared__ int s_i[8][16];
+struct RouteBlockSmem {
+  float g[256];  // group scores (n_group <= E / 2)
+  int kept[256];
+  float v[8][16], s[8][16];
+  int i[8][16];
+};
+
+// The routing of token t by 256 threads (tid = 0..255 within the group).  All
+// threads of the block call it the same number of times: it has three block
+// barriers; a group whose token is past T (active false) only joins them.
+__device__ __forceinline__ void route_block_body(const RouteArgs& a, int t, bool active, int tid,
+                                                 RouteBlockSmem& sm, int32_t* s_counts) {
+  float* s_g = sm.g;
+  int* s_kept = sm.kept;
+  auto& s_v = sm.v;
+  auto& s_s = sm.s;
+  auto& s_i = sm.i;
   const unsigned full = 0xffffffffu;
-  const int t = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lane = tid & 31, warp = tid >> 5;
   const int E = a.E, ng = a.n_group;
   const int gs = E / ng;
   const int e = tid;
-  const bool live = e < E;
+  const bool live = active && e < E;
   float s = 0.f, sb = -INFINITY;
   if (live) {
     float x;
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
   }
   if (live && e % gs == 0) s_g[e / gs] = __fadd_rn(t2.a, t2.b);
   __syncthreads();
-  if (warp == 0) {  // the topk_group best groups
+  if (active && warp == 0) {  // the topk_group best groups
     for (int g = lane; g < ng; g += 32) s_kept[g] = 0;
     __syncwarp();
     for (int it = 0; it < a.topk_group; ++it) {
@@ -271,7 +282,7 @@ __global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
     if (e == bi) cand = -INFINITY;
   }
   __syncthreads();
-  if (warp != 0) return;
+  if (!active || warp != 0) return;
   // warp 0: the global top-k from the 8 lists (lane holds entries lane, lane+32, ...)
   const int n = 8 * a.top_k;
   bool taken[4] = {false, false, false, false};
@@ -325,14 +336,21 @@ __global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
     a.topk_w[o] = __fmul_rn(__fdiv_rn(my_s, sum), a.rsf);
     if (a.pair_row) a.pair_row[o] = -1;
     const int le = my_e - a.local_offset;
-    if (a.counts && le >= 0 && le < a.E_local) atomicAdd(a.counts + le, 1);
+    if (le >= 0 && le < a.E_local) {
+      if (s_counts) atomicAdd(s_counts + le, 1);
+      else if (a.counts) atomicAdd(a.counts + le, 1);
+    }
   }
 }
 
+__global__ void __launch_bounds__(256) route_block_kernel(RouteArgs a) {
+  __shared__ RouteBlockSmem sm;
+  route_block_body(a, blockIdx.x, true, threadIdx.x, sm, nullptr);
+}
+
 // Single block: per-group exclusive offsets and the 128-row M-tile list.
-__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
-  __shared__ int s_tiles[1024];
-  __shared__ int s_rows[1024];
+// Needs blockDim.x == 1024 (the scan width); every thread of the block calls it.
+__device__ __forceinline__ void plan_block(const PlanArgs& a, int* s_tiles, int* s_rows) {
   const int groups = a.E_local + (a.shared_rows > 0 ? 1 : 0);
   const int tid = threadIdx.x;
   int rows_total = 0, tiles_total = 0;
@@ -384,6 +402,61 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     if (rows_total > a.row_capacity) {  // counts disagree with the buffers' size: do no GEMM work
       a.num_tiles[0] = 0;
       atomicOr(a.err, kErrRowOverflow);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
+  __shared__ int s_tiles[1024];
+  __shared__ int s_rows[1024];
+  plan_block(a, s_tiles, s_rows);
+}
+
+// Decode-sized batches (T <= kFrontMaxT): routing, plan and row assignment
+// in one 1024-thread block, four groups of 256 threads routing one token each
+// (route_block_body), then plan_block over the block's counts, then the rows
+// of each local expert in increasing token order.  The results are those of
+// route_block_kernel + plan_kernel + assign_kernel; the two launches and
+// kernel boundaries it saves are a large part of a decode step.
+constexpr int kFrontMaxT = 4;
+
+__global__ void __launch_bounds__(1024) decode_front_kernel(RouteArgs ra, PlanArgs pa, AssignArgs sa) {
+  __shared__ RouteBlockSmem rsm[kFrontMaxT];
+  __shared__ int32_t s_counts[256];
+  __shared__ int s_tiles[1024];
+  __shared__ int s_rows[1024];
+  const int tid = threadIdx.x;
+  if (tid < 256) s_counts[tid] = 0;
+  __syncthreads();
+  const int t = tid >> 8;  // this thread's token group
+  route_block_body(ra, t, t < ra.T, tid & 255, rsm[t], s_counts);
+  __syncthreads();
+  for (int i = tid; i < ra.E_local; i += blockDim.x) ra.counts[i] = s_counts[i];
+  __syncthreads();
+  plan_block(pa, s_tiles, s_rows);
+  __syncthreads();
+  const int K = sa.top_k;
+  if (tid < sa.T * K) {  // (token, slot): its rank among the tokens routed to the same expert
+    const int tt = tid / K, j = tid - tt * K;
+    const int e = sa.topk_idx[tt * K + j];
+    const int le = e - sa.local_offset;
+    if (e >= 0 && le >= 0 && le < sa.E_local) {
+      int rank = 0;
+      for (int tp = 0; tp < tt; ++tp)
+        for (int jp = 0; jp < K; ++jp) rank += sa.topk_idx[tp * K + jp] == e;
+      const int r = sa.offsets[le] + rank;
+      if (r < sa.row_capacity) {
+        sa.row_token[r] = tt;
+        sa.row_weight[r] = sa.topk_w[tt * K + j];
+        sa.pair_row[tt * K + j] = r;
+      }
+    }
+  }
+  if (sa.shared_rows > 0 && tid < sa.T) {
+    const int r = sa.offsets[sa.E_local] + tid;
+    if (r < sa.row_capacity) {
+      sa.row_token[r] = tid;
+      sa.row_weight[r] = 1.0f;
     }
   }
 }
@@ -471,6 +544,18 @@ int launch_route(const RouteArgs& a, cudaStream_t s) {
   }
   const int warps_per_block = 8;
   route_kernel<<<cdiv(a.T, warps_per_block), warps_per_block * 32, 0, s>>>(a);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+bool decode_front_ok(const RouteArgs& ra, const PlanArgs& pa) {
+  return ra.T >= 1 && ra.T <= kFrontMaxT && ra.E <= 256 && ra.top_k <= 16 && ra.E_local <= 256 &&
+         pa.E_local + (pa.shared_rows > 0 ? 1 : 0) <= 1024;
+}
+
+int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, cudaStream_t s) {
+  if (!decode_front_ok(ra, pa) || sa.idx_stride > 0 || sa.T_dev) return GEMMS_ERR_SHAPE;
+  decode_front_kernel<<<1, 1024, 0, s>>>(ra, pa, sa);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }
