@@ -655,18 +655,22 @@ def gpu_arm(a):
         row_b = H + 4 * H // 128
         inter_b = 2 * (planes * I + 4 * I // 128)
         R, P = ep_timeline["recv_rows"], ep_timeline["pair_rows"]
+        # the shared expert is in the roofline only where it has its own phase
+        # (with the device exchange it runs beside the gather, `shared_and_gather`)
+        shared_timed = sh.shared and ("shared_ffn" in ep_timeline or "shared_ffn_2" in ep_timeline)
         ffn_bytes = (ep_timeline["experts_hit"] * w_exp + P * (row_b + inter_b) + R * H * 4 * 2
-                     + ((w_exp + sh.T * (row_b + inter_b) + sh.T * H * 4 * 2) if sh.shared else 0))
+                     + ((w_exp + sh.T * (row_b + inter_b) + sh.T * H * 4 * 2) if shared_timed else 0))
         ffn_ms = ep_timeline["expert_ffn"] + (ep_timeline.get("shared_ffn", 0.0) + ep_timeline.get("shared_ffn_2", 0.0)
-                                              if sh.shared else 0.0)
+                                              if shared_timed else 0.0)
         ach = ffn_bytes / (ffn_ms / 1e3) / 1e9
         # at c3 the grouped rows per rank (>= 32k) make the FFN compute-bound:
         # its roof is the tensor pipe (FP8 work of rank 0's grouped rows and
         # shared rows over the same phases)
-        ffn_flops = 6.0 * H * I * (P + (sh.T if sh.shared else 0))
+        ffn_flops = 6.0 * H * I * (P + (sh.T if shared_timed else 0))
         ach_tf = ffn_flops / (ffn_ms / 1e3) / 1e12
-        line["roofline"] = {"bound": "tensor", "kernel": "grouped GEMM1+GEMM2 over received rows + shared expert "
-                                                         "(rank 0, expert_ffn + shared_ffn phases)",
+        line["roofline"] = {"bound": "tensor", "kernel": "grouped GEMM1+GEMM2 over received rows" +
+                                                         (" + shared expert (rank 0, expert_ffn + shared_ffn phases)"
+                                                          if shared_timed else " (rank 0, expert_ffn phase)"),
                             "achieved": ach_tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": ach_tf / fp8_peak,
                             "peak_source": "dense FP8 measured in this run (torch._scaled_mm, cuBLAS, e4m3 8192^3); "
                                            "MEASURED_PEAKS.json has no FP8 entry",

@@ -44,6 +44,8 @@ EXPORTS = (
     "gemms_ep_pack_back_dev",
     "gemms_ep_combine_peer",
     "gemms_ep_set_pull_ctas",
+    "gemms_ep_gather_add_peer",
+    "gemms_f32_to_bf16",
     "gemms_set_gemm_ctas",
     "gemms_moe_fwd_noalloc",
     "gemms_moe_check_noalloc",
@@ -179,6 +181,11 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_ep_combine_peer.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                             c_int32, c_void_p, c_void_p]
         L.gemms_ep_combine_peer.restype = c_int32
+        L.gemms_ep_gather_add_peer.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                               c_int32, c_void_p]
+        L.gemms_ep_gather_add_peer.restype = c_int32
+        L.gemms_f32_to_bf16.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+        L.gemms_f32_to_bf16.restype = c_int32
         L.gemms_ep_set_pull_ctas.argtypes = [c_int32]
         L.gemms_ep_set_pull_ctas.restype = c_int32
         L.gemms_moe_fwd_noalloc.argtypes = [ctypes.POINTER(GemmsMoeArgs), c_void_p]

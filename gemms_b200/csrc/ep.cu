@@ -248,9 +248,13 @@ struct BackRows {
   int cap;                 // > 0: rows at or past it are outside the buffers and are skipped
 };
 
+// out = bf16(acc + rows), or with add_to (acc, out unused): add_to += rows in
+// fp32 with one vector atomic per 4 columns (for a sum that other kernels add
+// into at the same time, e.g. the shared expert's GEMMs).
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ acc, const BackRows rows_at,
                                                          size_t rbb, const int32_t* __restrict__ send_row_of, int T,
-                                                         int H, int world, __nv_bfloat16* __restrict__ out) {
+                                                         int H, int world, __nv_bfloat16* __restrict__ out,
+                                                         float* __restrict__ add_to) {
   __shared__ const uint8_t* s_rows[kMaxWorld];
   __shared__ float s_scale[kMaxWorld];
   __shared__ int s_nd;
@@ -277,8 +281,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
   const int nd = s_nd;
   const uint8_t* const* rows = s_rows;
   const float* scale = s_scale;
+  if (add_to && nd == 0) return;
   for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
-    float4 s = *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
+    float4 s = add_to ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(acc + (size_t)t * H + c);
     for (int i = 0; i < nd; ++i) {
       const uint2 b = *reinterpret_cast<const uint2*>(rows[i] + 2 * (size_t)c);
       const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
@@ -287,6 +292,10 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
       s.y = fmaf(lo.y, scale[i], s.y);
       s.z = fmaf(hi.x, scale[i], s.z);
       s.w = fmaf(hi.y, scale[i], s.w);
+    }
+    if (add_to) {
+      atomicAdd(reinterpret_cast<float4*>(add_to + (size_t)t * H + c), s);
+      continue;
     }
     __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
     uint2 o;
@@ -725,9 +734,37 @@ int gemms_ep_combine_peer(const float* acc, const void* const* row_base, const i
   at.add_dev = info + kInfoAdd;
   at.cap = recv_cap;
   ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16), nullptr);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
+}
+
+int gemms_ep_gather_add_peer(float* acc, const void* const* row_base, const int32_t* info,
+                             const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, int32_t recv_cap,
+                             gemms_stream_t stream_) {
+  if (T < 0 || H <= 0 || H % 4 || world < 1 || world > kMaxWorld || recv_cap < 1) return GEMMS_ERR_SHAPE;
+  if (!acc || !send_row_of || !row_base || !info) return GEMMS_ERR_ARG;
+  if (!aligned16(acc)) return GEMMS_ERR_ALIGN;
+  if (T == 0) return GEMMS_OK;
+  BackRows at{};
+  for (int d = 0; d < world; ++d) {
+    if (row_base[d] && !aligned16(row_base[d])) return GEMMS_ERR_ALIGN;
+    at.base[d] = static_cast<const uint8_t*>(row_base[d]);
+  }
+  at.add_dev = info + kInfoAdd;
+  at.cap = recv_cap;
+  ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      nullptr, at, ep_back_row_bytes(H), send_row_of, T, H, world, nullptr, acc);
+  GEMMS_CUDA_TRY(cudaGetLastError());
+  return GEMMS_OK;
+}
+
+int gemms_f32_to_bf16(const float* in, void* out_bf16, size_t n, gemms_stream_t stream) {
+  if (n % 4) return GEMMS_ERR_SHAPE;
+  if (n == 0) return GEMMS_OK;
+  if (!in || !out_bf16) return GEMMS_ERR_ARG;
+  if (!aligned16(in) || (reinterpret_cast<uintptr_t>(out_bf16) & 7u)) return GEMMS_ERR_ALIGN;
+  return launch_to_bf16(in, static_cast<__nv_bfloat16*>(out_bf16), n, nullptr, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int gemms_ep_set_pull_ctas(int32_t ctas) {
@@ -757,7 +794,7 @@ int gemms_ep_combine(const float* acc, const void* back_packed, const int32_t* s
   BackRows at{};
   for (int d = 0; d < world; ++d) at.base[d] = static_cast<const uint8_t*>(back_packed);
   ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16), nullptr);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }
@@ -776,7 +813,7 @@ int gemms_ep_combine_rows(const float* acc, const void* const* row_base, const i
     at.add[d] = row_add[d];
   }
   ep_combine_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16));
+      acc, at, ep_back_row_bytes(H), send_row_of, T, H, world, static_cast<__nv_bfloat16*>(out_bf16), nullptr);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }

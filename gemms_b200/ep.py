@@ -300,6 +300,21 @@ class CudaEpKernels:
             self._ws[key] = st
         return st
 
+    def gather_add_peer(self, acc, region, info, send_row_of, world: int):
+        """acc fp32 [T, H] += this rank's combine rows read from every
+        destination's region, with atomics (``gemms_ep_gather_add_peer``)."""
+        T, H = acc.shape
+        bases = (ctypes.c_void_p * world)(*region.back_bases)
+        _lib.check(self.L.gemms_ep_gather_add_peer(acc.data_ptr(), bases, info.data_ptr(), send_row_of.data_ptr(), T,
+                                                   H, world, region.recv_cap, self._stream()),
+                   "gemms_ep_gather_add_peer")
+
+    def to_bf16(self, acc):
+        out = torch.empty(acc.shape, dtype=torch.bfloat16, device=acc.device)
+        _lib.check(self.L.gemms_f32_to_bf16(acc.data_ptr(), out.data_ptr(), acc.numel(), self._stream()),
+                   "gemms_f32_to_bf16")
+        return out
+
     def exchange_flags(self, region) -> int:
         """info[2] of the last pull (reads the device: synchronises)."""
         return int(region.info[2].item())
@@ -442,9 +457,12 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     # side stream beside the barriers, the pull and the routed experts (its
     # GEMMs leave GEMMS_EP_COMM_SMS SMs to the pull and NCCL), and the combine
     # waits for it.
-    side = K.side_stream() if shared[0] is not None and _peer_overlap() else None
+    combine_overlap = shared[0] is not None and _combine_overlap()
+    side = K.side_stream() if shared[0] is not None and (_peer_overlap() or combine_overlap) else None
+    if side is None:
+        combine_overlap = False
     done_shared = None
-    if side is not None:
+    if side is not None and not combine_overlap:
         ready = torch.cuda.Event()
         ready.record()
         side.wait_event(ready)
@@ -470,6 +488,28 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     mark("pack_back")
     K.peer_barrier(group, reg)  # every rank's combine rows are written
     mark("publish")
+    if combine_overlap:
+        # the NVLink-bound gather (side stream) beside the compute-bound shared
+        # expert (this stream, GEMMs bounded to leave SMs to the gather); both
+        # add into acc, then one cast
+        main = torch.cuda.current_stream()
+        ready = torch.cuda.Event()
+        ready.record()
+        with K.comm_overlap():
+            K.shared_ffn(xq, xq_scale, *shared, inter_planes, acc, 0)
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            for t in (acc, send_row_of):
+                t.record_stream(side)
+            K.gather_add_peer(acc, reg, info, send_row_of, world)
+            gathered = torch.cuda.Event()
+            gathered.record()
+        main.wait_event(gathered)
+        mark("shared_and_gather")
+        out = K.to_bf16(acc)
+        mark("cast")
+        _timeline_stats(timeline, stats)
+        return out
     if done_shared is not None:
         torch.cuda.current_stream().wait_event(done_shared)
         mark("shared_wait")
@@ -477,6 +517,13 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
     mark("gather")
     _timeline_stats(timeline, stats)
     return out
+
+
+def _combine_overlap() -> bool:
+    """exchange="peer": the shared expert runs after the second barrier beside
+    the gather of the result rows (default; GEMMS_EP_COMBINE_OVERLAP=0 runs
+    it before the routed experts and gathers afterwards)."""
+    return os.environ.get("GEMMS_EP_COMBINE_OVERLAP", "1") != "0"
 
 
 def _peer_overlap() -> bool:

@@ -304,6 +304,17 @@ int gemms_ep_combine_peer(const float* acc, const void* const* row_base, const i
                           const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, int32_t recv_cap,
                           void* out_bf16, gemms_stream_t stream);
 
+/* acc fp32 [T, H] += this rank's combine rows read in place from every
+ * destination's region (the same rows and offsets as gemms_ep_combine_peer),
+ * with fp32 vector atomics, so that other kernels (the shared expert's GEMMs)
+ * may add into acc at the same time; then gemms_f32_to_bf16 casts the sum. */
+int gemms_ep_gather_add_peer(float* acc, const void* const* row_base, const int32_t* info,
+                             const int32_t* send_row_of, int32_t T, int32_t H, int32_t world, int32_t recv_cap,
+                             gemms_stream_t stream);
+
+/* out bf16 [n] = in fp32 [n] rounded to nearest even; n a multiple of 4. */
+int gemms_f32_to_bf16(const float* in, void* out_bf16, size_t n, gemms_stream_t stream);
+
 /* CTAs of gemms_ep_pull's row copy for later calls (0 = two per SM, the
  * default); returns the previous value, or GEMMS_ERR_ARG if negative. */
 int gemms_ep_set_pull_ctas(int32_t ctas);

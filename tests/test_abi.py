@@ -141,6 +141,11 @@ def test_new_entry_points_validate_arguments_without_gpu():
     assert L.gemms_ep_combine_peer(None, bases, info, None, 4, 7168, 2, 0, None, None) == ERR_SHAPE
     assert L.gemms_ep_expert_ffn_dev(None, 4, None, 32, 7168, 2048, 8, 32, 0, 2, None, None, None, None, None,
                                      None, 0, None) == ERR_ARG
+    assert L.gemms_ep_gather_add_peer(None, bases, info, None, 4, 7168, 2, 8, None) == ERR_ARG
+    assert L.gemms_ep_gather_add_peer(None, bases, info, None, 4, 7168, 2, 0, None) == ERR_SHAPE
+    assert L.gemms_f32_to_bf16(None, None, 6, None) == ERR_SHAPE
+    assert L.gemms_f32_to_bf16(None, None, 0, None) == 0
+    assert L.gemms_f32_to_bf16(None, None, 8, None) == ERR_ARG
     assert L.gemms_ep_set_pull_ctas(-1) == ERR_ARG
     prev = L.gemms_ep_set_pull_ctas(16)
     assert L.gemms_ep_set_pull_ctas(prev) == 16
