@@ -520,10 +520,12 @@ def _moe_ep_peer(K, x, idx, wts, w13, w13_scale, w2, w2_scale, shared, group, wo
 
 
 def _combine_overlap() -> bool:
-    """exchange="peer": the shared expert runs after the second barrier beside
-    the gather of the result rows (default; GEMMS_EP_COMBINE_OVERLAP=0 runs
-    it before the routed experts and gathers afterwards)."""
-    return os.environ.get("GEMMS_EP_COMBINE_OVERLAP", "1") != "0"
+    """GEMMS_EP_COMBINE_OVERLAP=1 (exchange="peer"): the shared expert runs
+    after the second barrier beside the gather of the result rows.  Off by
+    default: at N=2 (c3, one box) the two together took 1.64-1.71 ms against
+    1.14 + 0.43 ms in sequence, plus a 0.12 ms cast, because the gather's
+    NVLink reads and the shared GEMMs slow each other down."""
+    return os.environ.get("GEMMS_EP_COMBINE_OVERLAP", "0") == "1"
 
 
 def _peer_overlap() -> bool:
