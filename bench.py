@@ -375,13 +375,13 @@ def count_kernels_per_step(step_fn) -> int:
     return n
 
 
-def decode_sweep(d, kw, sh, hbm, Ts=(1, 4, 8, 32, 128), steps=50, warmup=5):
+def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
     """BASELINE config c2: the same full layer (same weights) on the first T
     tokens, T in Ts, one GPU.  Decode streams the weights of every expert the
     batch hits (+ the shared expert), so each line reports that weight traffic
     per layer as HBM GB/s; the experts hit are counted from the batch's own
-    routing.  For T <= 4 (the CUDA-core expert GEMMs) the graph is also timed
-    with the tensor-core GEMMs (``gemms_set_decode_max_t(0)``) on the same box.  Every step reads >= 396 MB of weights (T=1: 8 experts + shared),
+    routing.  For T <= 4 the graph is also timed with the CUDA-core expert
+    GEMMs forced on and off (``gemms_set_decode_max_t``), an A/B on one box.  Every step reads >= 396 MB of weights (T=1: 8 experts + shared),
     more than the 126 MB L2."""
     import torch
 
@@ -416,30 +416,31 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 4, 8, 32, 128), steps=50, warmup=5):
         e1.synchronize()
         ms_g = e0.elapsed_time(e1) / steps
         del graph
-        ms_tc = None
-        if T <= 4:  # the same graph with the tensor-core GEMMs (decode path off), for an A/B on this box
+        ab = {}
+        if T <= 4:  # A/B on this box: the graph with the CUDA-core and with the tensor-core expert GEMMs
             L = gemms_b200.load_library()
-            prev = L.gemms_set_decode_max_t(0)
-            try:
-                graph = gemms_b200.MoeGraph(d, T, **kw)
-                for _ in range(warmup):
-                    graph(x)
-                torch.cuda.synchronize()
-                e0.record()
-                for _ in range(steps):
-                    graph(x)
-                e1.record()
-                e1.synchronize()
-                ms_tc = e0.elapsed_time(e1) / steps
-                del graph
-            finally:
-                L.gemms_set_decode_max_t(prev)
+            for name, limit in (("graph_cuda_core_gemms_ms", 4), ("graph_tensor_core_gemms_ms", 0)):
+                prev = L.gemms_set_decode_max_t(limit)
+                try:
+                    graph = gemms_b200.MoeGraph(d, T, **kw)
+                    for _ in range(warmup):
+                        graph(x)
+                    torch.cuda.synchronize()
+                    e0.record()
+                    for _ in range(steps):
+                        graph(x)
+                    e1.record()
+                    e1.synchronize()
+                    ab[name] = round(e0.elapsed_time(e1) / steps, 5)
+                    del graph
+                finally:
+                    L.gemms_set_decode_max_t(prev)
         nbytes = (hit + (1 if sh.shared else 0)) * sh.expert_bytes()
         gbs = nbytes / (ms / 1e3) / 1e9
         gbs_g = nbytes / (ms_g / 1e3) / 1e9
         res[f"T={T}"] = {"ms_per_step": round(ms, 5), "tokens_per_s": round(T / (ms / 1e3), 1), "experts_hit": hit,
                          "weight_bytes": nbytes, "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
-                         **({"graph_tensor_core_gemms_ms": round(ms_tc, 5)} if ms_tc is not None else {}),
+                         **ab,
                          "graph": {"ms_per_step": round(ms_g, 5), "tokens_per_s": round(T / (ms_g / 1e3), 1),
                                    "GB/s": round(gbs_g, 1), "hbm_frac": round(gbs_g / hbm, 4)}}
     return res

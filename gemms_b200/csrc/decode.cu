@@ -72,6 +72,18 @@ template <int MR>
 constexpr int ring_stages() { return MR >= 4 ? 2 : 4; }
 constexpr size_t ring_bytes(int stages) { return (size_t)kDecWarps * stages * kRowsPerWarp * 32 * 16; }
 
+// (a0, a1) += (w0, w1) * (x0, x1): one packed fp32x2 FMA for two weights.
+__device__ __forceinline__ void ffma2_vv(float& a0, float& a1, float w0, float w1, float x0, float x1) {
+  asm("{\n\t.reg .b64 acc, wv, xv;\n\t"
+      "mov.b64 acc, {%0, %1};\n\t"
+      "mov.b64 wv, {%2, %3};\n\t"
+      "mov.b64 xv, {%4, %5};\n\t"
+      "fma.rn.f32x2 acc, wv, xv, acc;\n\t"
+      "mov.b64 {%0, %1}, acc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(w0), "f"(w1), "f"(x0), "f"(x1));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -168,17 +180,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
       const int kb = c / (kBlock / kChunk);
       float part[kRowsPerWarp][MR];
 #pragma unroll
-      for (int q = 0; q < kRowsPerWarp; ++q)
-#pragma unroll
-        for (int r = 0; r < MR; ++r) part[q][r] = 0.f;
-#pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
         float f[kChunk];
         e4m3x16_to_f(wv[q], f);
+        float pe[MR], po[MR];  // even / odd elements, two per packed FMA
 #pragma unroll
-        for (int e = 0; e < kChunk; ++e)
+        for (int r = 0; r < MR; ++r) pe[r] = po[r] = 0.f;
 #pragma unroll
-          for (int r = 0; r < MR; ++r) part[q][r] = fmaf(f[e], sA[((size_t)r * kChunk + e) * NC + c], part[q][r]);
+        for (int e = 0; e < kChunk; e += 2)
+#pragma unroll
+          for (int r = 0; r < MR; ++r)
+            ffma2_vv(pe[r], po[r], f[e], f[e + 1], sA[((size_t)r * kChunk + e) * NC + c],
+                     sA[((size_t)r * kChunk + e + 1) * NC + c]);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) part[q][r] = pe[r] + po[r];
       }
 #pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
@@ -273,13 +288,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
       for (int q = 0; q < kRowsPerWarp; ++q) {
         float f[kChunk];
         e4m3x16_to_f(wv[q], f);
-        float part[MR];
+        float part[MR], pe[MR], po[MR];
 #pragma unroll
-        for (int r = 0; r < MR; ++r) part[r] = 0.f;
+        for (int r = 0; r < MR; ++r) pe[r] = po[r] = 0.f;
 #pragma unroll
-        for (int e = 0; e < kChunk; ++e)
+        for (int e = 0; e < kChunk; e += 2)
 #pragma unroll
-          for (int r = 0; r < MR; ++r) part[r] = fmaf(f[e], sC[((size_t)r * kChunk + e) * NC + c], part[r]);
+          for (int r = 0; r < MR; ++r)
+            ffma2_vv(pe[r], po[r], f[e], f[e + 1], sC[((size_t)r * kChunk + e) * NC + c],
+                     sC[((size_t)r * kChunk + e + 1) * NC + c]);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) part[r] = pe[r] + po[r];
         const float ws = __ldg(WS + (size_t)((h0 + q) / kBlock) * KB + kb);
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[q][r] = fmaf(part[r], ws, acc[q][r]);

@@ -29,11 +29,12 @@ struct FwdLayout {
 };
 
 // Largest batch that takes the CUDA-core expert GEMMs: GEMMS_DECODE_MAX_T at
-// load time (default 4 = kDecodeMaxRows; 0 keeps every batch on the tensor
-// cores), changed by gemms_set_decode_max_t.
+// load time (default 1: measured faster than the tensor cores at T=1 and
+// slower at T=4 on the same box; 0 keeps every batch on the tensor cores),
+// changed by gemms_set_decode_max_t (at most kDecodeMaxRows).
 std::atomic<int> g_decode_t_limit{[] {
   const char* e = std::getenv("GEMMS_DECODE_MAX_T");
-  const int x = e ? std::atoi(e) : kDecodeMaxRows;
+  const int x = e ? std::atoi(e) : 1;
   return std::max(0, std::min(x, kDecodeMaxRows));
 }()};
 int decode_t_limit() { return g_decode_t_limit.load(std::memory_order_relaxed); }

@@ -113,9 +113,10 @@ typedef struct {
 size_t gemms_moe_workspace_size(const GemmsMoeShape* shape);
 
 /* Batches of at most max_t tokens (<= 4) run the two expert GEMMs on the CUDA
- * cores as weight streams (with <= 4 rows per expert the tensor-core GEMMs are
- * bound by their per-K-block chain, not by HBM); 0 keeps every batch on the
- * tensor cores.  Default 4, or GEMMS_DECODE_MAX_T at library load.  The
+ * cores as weight streams (with so few rows per expert the tensor-core GEMMs
+ * are bound by their per-K-block chain, not by HBM); 0 keeps every batch on
+ * the tensor cores.  Default 1 (faster than the tensor cores at T=1, slower at
+ * T=4, measured on one box), or GEMMS_DECODE_MAX_T at library load.  The
  * workspace size depends on it: query gemms_moe_workspace_size after setting
  * it.  Returns the previous value, or GEMMS_ERR_ARG if negative.  No
  * counterpart in the reference. */
