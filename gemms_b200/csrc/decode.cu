@@ -241,10 +241,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
     const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
     if (tile != staged) {
       __syncthreads();
-      for (int i = threadIdx.x; i < MR * I; i += blockDim.x) {
-        const int r = i / I, k = i - r * I;  // consecutive threads: consecutive k (coalesced global reads)
-        const int c = k / kChunk, e = k - c * kChunk;
-        sC[((size_t)r * kChunk + e) * NC + c] = r < rows ? inter[(size_t)(row0 + r) * I + k] : 0.f;
+      for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {  // thread per (row, 16-column chunk)
+        const int r = i / NC, c = i - r * NC;
+        float4 v[kChunk / 4];
+#pragma unroll
+        for (int q = 0; q < kChunk / 4; ++q)
+          v[q] = r < rows ? reinterpret_cast<const float4*>(inter + (size_t)(row0 + r) * I + (size_t)c * kChunk)[q]
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float* f = reinterpret_cast<const float*>(v);
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) sC[((size_t)r * kChunk + e) * NC + c] = f[e];  // consecutive c: no conflicts
       }
       __syncthreads();
       staged = tile;
