@@ -380,7 +380,7 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
     tokens, T in Ts, one GPU.  Decode streams the weights of every expert the
     batch hits (+ the shared expert), so each line reports that weight traffic
     per layer as HBM GB/s; the experts hit are counted from the batch's own
-    routing.  For T <= 4 the graph is also timed with the CUDA-core expert
+    routing.  For T <= 2 the graph is also timed with the CUDA-core expert
     GEMMs forced on and off (``gemms_set_decode_max_t``), an A/B on one box.  Every step reads >= 396 MB of weights (T=1: 8 experts + shared),
     more than the 126 MB L2."""
     import torch
@@ -417,9 +417,9 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
         ms_g = e0.elapsed_time(e1) / steps
         del graph
         ab = {}
-        if T <= 4:  # A/B on this box: the graph with the CUDA-core and with the tensor-core expert GEMMs
+        if T <= 2:  # A/B on this box: the graph with the CUDA-core and with the tensor-core expert GEMMs
             L = gemms_b200.load_library()
-            for name, limit in (("graph_cuda_core_gemms_ms", 4), ("graph_tensor_core_gemms_ms", 0)):
+            for name, limit in (("graph_cuda_core_gemms_ms", 2), ("graph_tensor_core_gemms_ms", 0)):
                 prev = L.gemms_set_decode_max_t(limit)
                 try:
                     graph = gemms_b200.MoeGraph(d, T, **kw)

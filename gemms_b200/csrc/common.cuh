@@ -155,10 +155,11 @@ struct Gemm2Args {
 int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
 
 // Decode-sized batches (decode.cu): the two expert GEMMs on the CUDA cores for
-// tiles of at most max_rows (<= kDecodeMaxRows) rows; GEMM1 writes the SwiGLU
+// tiles of at most max_rows (<= kDecodeMaxRows) rows (with more rows per
+// expert the FMA work per weight byte makes the tensor cores faster); GEMM1 writes the SwiGLU
 // output in fp32 to inter [R, I], GEMM2 reads it (same Gemm*Args as the
 // tensor-core path; the planes / inter / inter_scale fields are unused).
-constexpr int kDecodeMaxRows = 4;
+constexpr int kDecodeMaxRows = 2;
 bool decode_shape_ok(int H, int I);
 int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, cudaStream_t s);
 int launch_decode_gemm2(const Gemm2Args& g2, const float* inter, int max_rows, cudaStream_t s);

@@ -1,11 +1,11 @@
-// decode.cu -- the two expert GEMMs for decode-sized batches (T <= 4) on the
+// decode.cu -- the two expert GEMMs for decode-sized batches (T <= 2) on the
 // CUDA cores.
 //
-// With at most 4 rows per expert the tensor-core GEMMs (grouped_gemm.cu) run
+// With at most 2 rows per expert the tensor-core GEMMs (grouped_gemm.cu) run
 // each M tile as one long chain of 128-deep K blocks per CTA, MMA -> TMEM ->
 // promotion -> MMA, and at T=1 that chain, not HBM, sets their time (GEMM1:
 // one 56-block chain per CTA).  Here the work is a weight stream: every weight
-// byte is read once, converted from e4m3 and multiplied into <= 4 activation
+// byte is read once, converted from e4m3 and multiplied into <= 2 activation
 // rows held in shared memory, with many 16-byte loads in flight per SM, so the
 // time is the HBM time of the weights of the experts hit.
 //
@@ -19,7 +19,7 @@
 // output row (or stores the row for the deterministic combine).
 //
 // Work: the M-tile list of plan_kernel (one tile per hit expert, since rows
-// <= 4 < 128); a unit is (tile, a chunk of output rows); each CTA takes a
+// <= 2 < 128); a unit is (tile, a chunk of output rows); each CTA takes a
 // contiguous range of units, so it re-stages the activation rows only when the
 // tile changes.  Shared memory holds the activation rows as fp32 in a
 // [row][element-in-chunk][chunk] layout: lane c of a warp reads chunk c, so a
@@ -243,14 +243,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm2_kernel(Gemm2Args 
       __syncthreads();
       for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {  // thread per (row, 16-column chunk)
         const int r = i / NC, c = i - r * NC;
-        float4 v[kChunk / 4];
 #pragma unroll
-        for (int q = 0; q < kChunk / 4; ++q)
-          v[q] = r < rows ? reinterpret_cast<const float4*>(inter + (size_t)(row0 + r) * I + (size_t)c * kChunk)[q]
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float* f = reinterpret_cast<const float*>(v);
-#pragma unroll
-        for (int e = 0; e < kChunk; ++e) sC[((size_t)r * kChunk + e) * NC + c] = f[e];  // consecutive c: no conflicts
+        for (int q = 0; q < kChunk / 4; ++q) {  // consecutive c: conflict-free stores
+          const float4 v = r < rows
+                               ? reinterpret_cast<const float4*>(inter + (size_t)(row0 + r) * I + (size_t)c * kChunk)[q]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+          sC[((size_t)r * kChunk + 4 * q) * NC + c] = v.x;
+          sC[((size_t)r * kChunk + 4 * q + 1) * NC + c] = v.y;
+          sC[((size_t)r * kChunk + 4 * q + 2) * NC + c] = v.z;
+          sC[((size_t)r * kChunk + 4 * q + 3) * NC + c] = v.w;
+        }
       }
       __syncthreads();
       staged = tile;
@@ -389,15 +391,13 @@ int shape_ok(int H, int I) {
 int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, cudaStream_t s) {
   if (max_rows < 1 || max_rows > kDecodeMaxRows || !shape_ok(g1.H, g1.I)) return GEMMS_ERR_SHAPE;
   if (max_rows == 1) return launch_gemm1_mr<1>(g1, inter, s);
-  if (max_rows == 2) return launch_gemm1_mr<2>(g1, inter, s);
-  return launch_gemm1_mr<4>(g1, inter, s);
+  return launch_gemm1_mr<2>(g1, inter, s);
 }
 
 int launch_decode_gemm2(const Gemm2Args& g2, const float* inter, int max_rows, cudaStream_t s) {
   if (max_rows < 1 || max_rows > kDecodeMaxRows || !shape_ok(g2.H, g2.I)) return GEMMS_ERR_SHAPE;
   if (max_rows == 1) return launch_gemm2_mr<1>(g2, inter, s);
-  if (max_rows == 2) return launch_gemm2_mr<2>(g2, inter, s);
-  return launch_gemm2_mr<4>(g2, inter, s);
+  return launch_gemm2_mr<2>(g2, inter, s);
 }
 
 bool decode_shape_ok(int H, int I) { return shape_ok(H, I); }

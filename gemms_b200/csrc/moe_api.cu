@@ -77,7 +77,7 @@ FwdLayout fwd_layout(const GemmsMoeShape& s) {
   L.inter_scale = take(sizeof(float) * (size_t)(L.I / kBlock) * L.scale_ld);
   L.decode_rows = 0;
   if (s.T >= 1 && s.T <= decode_t_limit() && decode_shape_ok(s.H, s.I))
-    L.decode_rows = s.T <= 1 ? 1 : (s.T <= 2 ? 2 : 4);  // tiles hold <= T rows (routed and shared)
+    L.decode_rows = s.T <= 1 ? 1 : 2;  // tiles hold <= T rows (routed and shared)
   if (L.decode_rows) L.dec_inter = take(sizeof(float) * (size_t)std::max(L.R_max, 1) * L.I);
   L.det = s.deterministic ? 1 : 0;
   if (L.det)

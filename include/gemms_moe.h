@@ -112,7 +112,7 @@ typedef struct {
 /* Bytes of device workspace gemms_moe_fwd needs for this shape. */
 size_t gemms_moe_workspace_size(const GemmsMoeShape* shape);
 
-/* Batches of at most max_t tokens (<= 4) run the two expert GEMMs on the CUDA
+/* Batches of at most max_t tokens (<= 2) run the two expert GEMMs on the CUDA
  * cores as weight streams (with so few rows per expert the tensor-core GEMMs
  * are bound by their per-K-block chain, not by HBM); 0 keeps every batch on
  * the tensor cores.  Default 1 (faster than the tensor cores at T=1, slower at

@@ -1,4 +1,4 @@
-"""GPU: decode-sized batches (T <= 4) run the expert GEMMs on the CUDA cores
+"""GPU: decode-sized batches (T <= 2) run the expert GEMMs on the CUDA cores
 (csrc/decode.cu).  Every token is checked against the oracle, and the output
 is compared with the tensor-core path on the same inputs
 (``gemms_set_decode_max_t(0)``); the deterministic combine and the residual
@@ -41,7 +41,7 @@ def decode_limit():
     L.gemms_set_decode_max_t(prev)
 
 
-@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("T", [1, 2, 3])
 def test_decode_path_matches_oracle_and_tensor_path(decode_limit, T):
     L = decode_limit
     sh = W.CONFIGS["c2"].replace(T=T)
@@ -73,9 +73,10 @@ def test_decode_path_matches_oracle_and_tensor_path(decode_limit, T):
 
 
 def test_decode_path_small_geometry_and_residual(decode_limit):
-    """c0 geometry (H=2048, I=768, E=32) with a residual, T=1..4 in a row."""
+    """c0 geometry (H=2048, I=768, E=32) with a residual, T=1..3 in a row
+    (T=3 past the CUDA-core limit: the tensor cores take it)."""
     sh0 = W.CONFIGS["c0"].replace(shared=True)
-    for T in (1, 2, 3, 4):
+    for T in (1, 2, 3):
         sh = sh0.replace(T=T)
         d = W.make_inputs(sh, seed=40 + T, device="cuda")
         g = torch.Generator(device="cuda").manual_seed(T)
