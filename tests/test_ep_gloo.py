@@ -83,6 +83,59 @@ def test_ep_ranks_match_single_process_oracle(exchange, world):
     assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, m
 
 
+def _ragged_worker(rank, world, port, outdir):
+    """Ranks hold different token counts (ragged split of the 48 tokens) and
+    pass the same max_tokens_per_rank, as the device-driven exchange requires."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from tests.ep_fakes import CpuEpKernels
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    d = _inputs()
+    bounds = [0, 7, 30, 41, SHAPE.T] if world == 4 else [0, 31, SHAPE.T]
+    sl = slice(bounds[rank], bounds[rank + 1])
+    El = SHAPE.E // world
+    el = slice(rank * El, (rank + 1) * El)
+    K = CpuEpKernels(SHAPE.n_group, SHAPE.topk_group, SHAPE.top_k)
+    kw = dict(shared_w13=d["shared_w13"], shared_w13_scale=d["shared_w13_scale"], shared_w2=d["shared_w2"],
+              shared_w2_scale=d["shared_w2_scale"], n_group=SHAPE.n_group, topk_group=SHAPE.topk_group,
+              top_k=SHAPE.top_k, routed_scaling_factor=SHAPE.rsf, group=dist.group.WORLD, kernels=K,
+              exchange="peer")
+    wts = (d["w13"][el], d["w13_scale"][el], d["w2"][el], d["w2_scale"][el])
+    out = EP.moe_ep(d["x"][sl], d["router_w"], d["router_bias"], *wts, max_tokens_per_rank=SHAPE.T, **kw)
+    torch.save(out, os.path.join(outdir, f"out{rank}.pt"))
+    # more tokens than the stated capacity: refused on the host before any collective
+    err = ""
+    try:
+        EP.moe_ep(d["x"][sl], d["router_w"], d["router_bias"], *wts, max_tokens_per_rank=0, **kw)
+    except ValueError as e:
+        err = str(e)
+    with open(os.path.join(outdir, f"err{rank}.txt"), "w") as f:
+        f.write(err)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_ragged_ranks_with_capacity(world):
+    """Ragged token counts per rank under one max_tokens_per_rank: the plan
+    (receive order, offsets in the senders' regions, combine offsets) still
+    matches the single-process oracle; a rank past the capacity raises."""
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_ragged_worker, args=(world, _free_port(), tmp), nprocs=world, join=True)
+        got = torch.cat([torch.load(os.path.join(tmp, f"out{r}.pt")) for r in range(world)])
+        errs = [open(os.path.join(tmp, f"err{r}.txt")).read() for r in range(world)]
+    d = _inputs()
+    ref = R.moe_layer(d["x"], d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"],
+                      d["shared_w13"], d["shared_w13_scale"], d["shared_w2"], d["shared_w2_scale"],
+                      n_group=SHAPE.n_group, topk_group=SHAPE.topk_group, top_k=SHAPE.top_k, rsf=SHAPE.rsf)
+    m = R.compare(got, ref)
+    assert m["mae_rms"] < 3e-4 and m["max_rel"] < 1e-2, m
+    assert all("max_tokens_per_rank" in e for e in errs), errs
+
+
 def test_pack_back_round_trip():
     """Packed combine rows: exact power-of-two scale, fp16 rounding only, edge rows."""
     from tests.ep_fakes import CpuEpKernels
