@@ -66,6 +66,14 @@ def _worker(rank, world, port, outdir, case, exchange="nccl"):
         o = gemms_b200.moe(x_all[rank * tpr:(rank + 1) * tpr].contiguous(), d["router_w"], d["router_bias"], *wts,
                            ep_group=dist.group.WORLD, **kw)
         seq.append((x_all, o))
+    # ragged token counts per rank (world 2) under one max_tokens_per_rank
+    g = torch.Generator(device=dev).manual_seed(200)
+    x_all = torch.randn((2 * T, sh.H), generator=g, device=dev).to(torch.bfloat16)
+    cut = T // 3 + 1
+    part = x_all[:cut] if rank == 0 else x_all[cut:]
+    o = gemms_b200.moe(part.contiguous(), d["router_w"], d["router_bias"], *wts, ep_group=dist.group.WORLD,
+                       max_tokens_per_rank=2 * T, **kw)
+    seq.append((x_all, o))
     torch.cuda.synchronize()
     if exchange == "peer":  # no capacity or count flag raised by any pull
         from gemms_b200 import ep as EPm
