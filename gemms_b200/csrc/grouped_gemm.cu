@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           if (c == 2) {
             // The buffer's last columns are in registers: release it to the
-            // MMA before this round's FMAs (shortens the MMA -> promotion ->
+            // MMA before these columns' FMAs (shortens the MMA -> promotion ->
             // MMA hand-off by the FMA time).
             tc_fence_before();
             __syncwarp();
