@@ -90,7 +90,9 @@ int launch_assign(const AssignArgs& a, cudaStream_t s);
 // Decode-sized batches (T <= 4): route + plan + assign in one launch, same
 // results as launch_route, launch_plan and launch_assign in sequence.
 bool decode_front_ok(const RouteArgs& ra, const PlanArgs& pa);
-int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, cudaStream_t s);
+// zero_buf (optional, zero_n floats) is cleared by the same kernel.
+int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, float* zero_buf,
+                        size_t zero_n, cudaStream_t s);
 
 // Gather (and for bf16 input, quantise per 1x128) activation rows into the
 // expert-grouped operand: rows_fp8 [R, H], rows_scale [H/128, ld].
@@ -161,7 +163,17 @@ int launch_gemm2(const Gemm2Args& a, cudaStream_t s);
 // tensor-core path; the planes / inter / inter_scale fields are unused).
 constexpr int kDecodeMaxRows = 2;
 bool decode_shape_ok(int H, int I);
-int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, cudaStream_t s);
+// With row_token set, GEMM1 reads its activation rows straight from the
+// layer's input (token row_token[grouped row]; bf16 quantised per 1x128 as
+// permute_kernel does, or e4m3 + [H/128, T] scales) instead of g1.a / a_scale.
+struct DecodeSrc {
+  const int32_t* row_token;
+  const __nv_bfloat16* x_bf16;
+  const uint8_t* x_fp8;
+  const float* x_scale;
+  int T;
+};
+int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, const DecodeSrc* src, cudaStream_t s);
 int launch_decode_gemm2(const Gemm2Args& g2, const float* inter, int max_rows, cudaStream_t s);
 
 // Deterministic combine: out[t] = round(residual[t] + sum over j < K of

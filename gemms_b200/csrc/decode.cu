@@ -99,8 +99,32 @@ __device__ __forceinline__ void unit_range(int total, int& u0, int& u1) {
 
 // GEMM1 + SwiGLU.  Unit = (tile, 32 intermediate columns j); warp w takes
 // columns j0 + 2w and j0 + 2w + 1 (their gate rows j and up rows j + I).
+// A 128-column block of one activation row, quantised per 1x128 exactly as
+// permute_kernel does it: scale = amax / 448 (IEEE division), values
+// v / scale (IEEE) rounded to e4m3 with saturation.  The 8 threads of a block
+// (consecutive lanes) each hold 16 values and exchange their amax.
+__device__ __forceinline__ float quantise16(float* f, bool valid) {
+  float amax = 0.f;
+#pragma unroll
+  for (int e = 0; e < kChunk; ++e) amax = fmaxf(amax, fabsf(f[e]));
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float scale = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+#pragma unroll
+  for (int e = 0; e < kChunk; e += 2) {
+    const __nv_fp8x2_storage_t q = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fdiv_rn(f[e], scale), __fdiv_rn(f[e + 1], scale)), __NV_SATFINITE, __NV_E4M3);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(q, __NV_E4M3);
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    f[e] = valid ? d.x : 0.f;
+    f[e + 1] = valid ? d.y : 0.f;
+  }
+  return valid ? scale : 0.f;
+}
+
 template <int MR>
-__global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter) {
+__global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args a, float* __restrict__ inter,
+                                                                      DecodeSrc src) {
   extern __shared__ float smem[];
   const int H = a.H, I = a.I, KB = H / kBlock, NC = H / kChunk;
   float* sA = smem;                        // [MR][16][NC]
@@ -119,21 +143,59 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_gemm1_kernel(Gemm1Args 
     const int g = a.g.tile_group[tile], row0 = a.g.tile_row0[tile], rows = min(a.g.tile_rows[tile], MR);
     if (tile != staged) {
       __syncthreads();  // previous tile's rows no longer read
-      for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
-        const int r = i / NC, c = i - r * NC;
-        float f[kChunk];
-        if (r < rows) {
-          e4m3x16_to_f(*reinterpret_cast<const uint4*>(a.a + (size_t)(row0 + r) * H + (size_t)c * kChunk), f);
-        } else {
+      if (src.row_token) {
+        // rows straight from the layer's input (token row_token[r]): no
+        // permuted copy; whole warps iterate together for the amax exchange
+        for (int i0 = 0; i0 < MR * NC; i0 += blockDim.x) {
+          const int i = i0 + threadIdx.x;
+          const int r = min(i / NC, MR - 1), c = i - (i / NC) * NC;
+          const bool valid = i < MR * NC && r < rows;
+          const int tok = valid ? src.row_token[row0 + r] : 0;
+          float f[kChunk];
+          float scale = 0.f;
+          if (src.x_bf16) {
+            const uint4* p = reinterpret_cast<const uint4*>(src.x_bf16 + (size_t)tok * H + (size_t)c * kChunk);
+            const uint4 w0 = valid ? p[0] : make_uint4(0, 0, 0, 0), w1 = valid ? p[1] : make_uint4(0, 0, 0, 0);
+            const uint32_t u[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
+            for (int k2 = 0; k2 < 8; ++k2) {
+              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[k2]));
+              f[2 * k2] = v.x;
+              f[2 * k2 + 1] = v.y;
+            }
+            scale = quantise16(f, valid);
+          } else {
+            if (valid) {
+              e4m3x16_to_f(*reinterpret_cast<const uint4*>(src.x_fp8 + (size_t)tok * H + (size_t)c * kChunk), f);
+              scale = src.x_scale[(size_t)(c / (kBlock / kChunk)) * src.T + tok];
+            } else {
+#pragma unroll
+              for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
+            }
+          }
+          if (i < MR * NC) {
+#pragma unroll
+            for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
+            if ((c & (kBlock / kChunk - 1)) == 0) sS[r * KB + c / (kBlock / kChunk)] = scale;
+          }
         }
+      } else {
+        for (int i = threadIdx.x; i < MR * NC; i += blockDim.x) {
+          const int r = i / NC, c = i - r * NC;
+          float f[kChunk];
+          if (r < rows) {
+            e4m3x16_to_f(*reinterpret_cast<const uint4*>(a.a + (size_t)(row0 + r) * H + (size_t)c * kChunk), f);
+          } else {
 #pragma unroll
-        for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
-      }
-      for (int i = threadIdx.x; i < MR * KB; i += blockDim.x) {
-        const int r = i / KB, kb = i - r * KB;
-        sS[i] = r < rows ? a.a_scale[(size_t)kb * a.a_scale_ld + row0 + r] : 0.f;
+            for (int e = 0; e < kChunk; ++e) f[e] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < kChunk; ++e) sA[((size_t)r * kChunk + e) * NC + c] = f[e];
+        }
+        for (int i = threadIdx.x; i < MR * KB; i += blockDim.x) {
+          const int r = i / KB, kb = i - r * KB;
+          sS[i] = r < rows ? a.a_scale[(size_t)kb * a.a_scale_ld + row0 + r] : 0.f;
+        }
       }
       __syncthreads();
       staged = tile;
@@ -354,7 +416,7 @@ int allow_smem(K kernel, std::atomic<uint32_t>& done) {
 }
 
 template <int MR>
-int launch_gemm1_mr(const Gemm1Args& g1, float* inter, cudaStream_t s) {
+int launch_gemm1_mr(const Gemm1Args& g1, float* inter, const DecodeSrc& src, cudaStream_t s) {
   static std::atomic<uint32_t> done{0};
   const size_t smem = ((sizeof(float) * ((size_t)MR * g1.H + (size_t)MR * (g1.H / kBlock)) + 15) & ~(size_t)15) +
                       ring_bytes(ring_stages<MR>());
@@ -362,7 +424,7 @@ int launch_gemm1_mr(const Gemm1Args& g1, float* inter, cudaStream_t s) {
   if ((rc = allow_smem(decode_gemm1_kernel<MR>, done))) return rc;
   // one CTA of 16 warps per SM, each lane keeping S - 1 chunks of four weight
   // rows in flight through its ring
-  decode_gemm1_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g1, inter);
+  decode_gemm1_kernel<MR><<<num_sms(), kDecThreads, smem, s>>>(g1, inter, src);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }
@@ -388,10 +450,13 @@ int shape_ok(int H, int I) {
 
 }  // namespace
 
-int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, cudaStream_t s) {
+int launch_decode_gemm1(const Gemm1Args& g1, float* inter, int max_rows, const DecodeSrc* src, cudaStream_t s) {
   if (max_rows < 1 || max_rows > kDecodeMaxRows || !shape_ok(g1.H, g1.I)) return GEMMS_ERR_SHAPE;
-  if (max_rows == 1) return launch_gemm1_mr<1>(g1, inter, s);
-  return launch_gemm1_mr<2>(g1, inter, s);
+  const DecodeSrc none{};
+  const DecodeSrc& sr = src ? *src : none;
+  if (sr.row_token && !sr.x_bf16 && !(sr.x_fp8 && sr.x_scale)) return GEMMS_ERR_ARG;
+  if (max_rows == 1) return launch_gemm1_mr<1>(g1, inter, sr, s);
+  return launch_gemm1_mr<2>(g1, inter, sr, s);
 }
 
 int launch_decode_gemm2(const Gemm2Args& g2, const float* inter, int max_rows, cudaStream_t s) {

@@ -188,7 +188,10 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   void* ws = workspace;
   int* err = at<int>(ws, L.err);
   GEMMS_CUDA_TRY(cudaMemsetAsync(ws, 0, L.head_bytes, st));
-  if (!L.det) GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
+  // (the decode front kernel zeroes the accumulator itself)
+  const bool fused_front = L.decode_rows > 0;
+  if (!L.det && !fused_front)
+    GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
 
   RouteArgs ra{};
   if (gemm_router) {
@@ -254,9 +257,12 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   sa.pair_row = ra.pair_row;
   sa.shared_rows = pa.shared_rows;
   sa.row_capacity = L.R_max;
-  if (L.decode_rows && decode_front_ok(ra, pa)) {
-    if ((rc = launch_decode_front(ra, pa, sa, st))) return rc;
+  if (fused_front && decode_front_ok(ra, pa)) {
+    if ((rc = launch_decode_front(ra, pa, sa, L.det ? nullptr : at<float>(ws, L.out_acc), (size_t)L.T * L.H, st)))
+      return rc;
   } else {
+    if (fused_front && !L.det)
+      GEMMS_CUDA_TRY(cudaMemsetAsync(at<char>(ws, L.out_acc), 0, sizeof(float) * (size_t)L.T * L.H, st));
     if ((rc = launch_route(ra, st))) return rc;
     if ((rc = launch_plan(pa, st))) return rc;
     if ((rc = launch_assign(sa, st))) return rc;
@@ -275,7 +281,17 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   qa.rows_fp8 = at<uint8_t>(ws, L.a_rows);
   qa.rows_scale = at<float>(ws, L.a_scale);
   qa.scale_ld = L.scale_ld;
-  if ((rc = launch_permute(qa, st))) return rc;
+  // the CUDA-core decode GEMM1 reads the input rows itself (no permuted copy)
+  DecodeSrc dsrc{};
+  if (L.decode_rows) {
+    dsrc.row_token = sa.row_token;
+    dsrc.x_bf16 = s.input_mode == GEMMS_INPUT_BF16 ? qa.x_bf16 : nullptr;
+    dsrc.x_fp8 = qa.x_fp8;
+    dsrc.x_scale = qa.x_scale;
+    dsrc.T = s.T;
+  } else if ((rc = launch_permute(qa, st))) {
+    return rc;
+  }
 
   GemmGroupsArgs gg{};
   gg.tile_group = pa.tile_group;
@@ -308,7 +324,7 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   cudaEvent_t const* evs = reinterpret_cast<cudaEvent_t const*>(args->profile_events);
   float* dec_inter = L.decode_rows ? at<float>(ws, L.dec_inter) : nullptr;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[0], st));
-  if ((rc = L.decode_rows ? launch_decode_gemm1(g1, dec_inter, L.decode_rows, st) : launch_gemm1(g1, st))) return rc;
+  if ((rc = L.decode_rows ? launch_decode_gemm1(g1, dec_inter, L.decode_rows, &dsrc, st) : launch_gemm1(g1, st))) return rc;
   if (evs) GEMMS_CUDA_TRY(cudaEventRecord(evs[1], st));
 
   Gemm2Args g2{};

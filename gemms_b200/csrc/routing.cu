@@ -252,61 +252,50 @@ __device__ __forceinline__ void route_block_body(const RouteArgs& a, int t, bool
     }
   }
   __syncthreads();
-  // each warp: top-k of its 32 candidates
-  float cand = (live && s_kept[e / gs]) ? sb : -INFINITY;
-  for (int it = 0; it < a.top_k; ++it) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    float bs = 0.f;
-    if (cand > bv) {
-      bv = cand;
-      bi = e;
-      bs = s;
-    }
+  // each warp: its 32 candidates sorted best first by (biased score desc,
+  // expert index asc) with a bitonic network; lanes < top_k hold its top-k.
+  // Non-candidates carry (-inf, 0x7fffffff, 0), the value route_kernel's
+  // selection reports once no candidate is left.
+  float v = (live && s_kept[e / gs]) ? sb : -INFINITY;
+  int vi = v > -INFINITY ? e : 0x7fffffff;
+  float vs = v > -INFINITY ? s : 0.f;
+  auto better = [](float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); };
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(full, bv, off);
-      const int oi = __shfl_xor_sync(full, bi, off);
-      const float os = __shfl_xor_sync(full, bs, off);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-        bs = os;
+  for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      const float ov = __shfl_xor_sync(full, v, j);
+      const int oi = __shfl_xor_sync(full, vi, j);
+      const float os = __shfl_xor_sync(full, vs, j);
+      const bool lower = (lane & j) == 0, best_first = (lane & kk) == 0;
+      const bool take = (lower == best_first) ? better(ov, oi, v, vi) : better(v, vi, ov, oi);
+      if (take) {
+        v = ov;
+        vi = oi;
+        vs = os;
       }
     }
-    if (lane == 0) {
-      s_v[warp][it] = bv;
-      s_i[warp][it] = bi;
-      s_s[warp][it] = bs;
-    }
-    if (e == bi) cand = -INFINITY;
+  }
+  if (lane < a.top_k) {
+    s_v[warp][lane] = v;
+    s_i[warp][lane] = vi;
+    s_s[warp][lane] = vs;
   }
   __syncthreads();
   if (!active || warp != 0) return;
-  // warp 0: the global top-k from the 8 lists (lane holds entries lane, lane+32, ...)
-  const int n = 8 * a.top_k;
-  bool taken[4] = {false, false, false, false};
+  // warp 0: merge the 8 sorted lists, lane w < 8 holding list w's head
+  int head = 0;
   int my_e = -1;
   float my_s = 0.f;
   for (int it = 0; it < a.top_k; ++it) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    float bs = 0.f;
+    const bool has = lane < 8 && head < a.top_k;
+    float bv = has ? s_v[lane & 7][head] : -INFINITY;
+    int bi = has ? s_i[lane & 7][head] : 0x7fffffff;
+    float bs = has ? s_s[lane & 7][head] : 0.f;
+    const float pv = bv;
+    const int pi = bi;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int m = lane + 32 * q;
-      if (m < n && !taken[q]) {
-        const float v = s_v[m / a.top_k][m % a.top_k];
-        const int i = s_i[m / a.top_k][m % a.top_k];
-        if (v > bv || (v == bv && v > -INFINITY && i < bi)) {
-          bv = v;
-          bi = i;
-          bs = s_s[m / a.top_k][m % a.top_k];
-        }
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
+    for (int off = 4; off > 0; off >>= 1) {  // within lanes 0-7 (and within each later group of 8)
       const float ov = __shfl_xor_sync(full, bv, off);
       const int oi = __shfl_xor_sync(full, bi, off);
       const float os = __shfl_xor_sync(full, bs, off);
@@ -316,15 +305,16 @@ __device__ __forceinline__ void route_block_body(const RouteArgs& a, int t, bool
         bs = os;
       }
     }
+    bv = __shfl_sync(full, bv, 0);
+    bi = __shfl_sync(full, bi, 0);
+    bs = __shfl_sync(full, bs, 0);
     if (lane == it) {
       my_e = bi;
       my_s = bs;
     }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int m = lane + 32 * q;
-      if (m < n && !taken[q] && bv > -INFINITY && s_i[m / a.top_k][m % a.top_k] == bi) taken[q] = true;
-    }
+    // the list that supplied the winner moves on (lowest such lane for fillers)
+    const unsigned hit = __ballot_sync(full, lane < 8 && pv == bv && pi == bi);
+    if (hit && lane == __ffs(hit) - 1) ++head;
   }
   float sum = (lane < a.top_k) ? my_s : 0.f;
 #pragma unroll
@@ -420,13 +410,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
 // kernel boundaries it saves are a large part of a decode step.
 constexpr int kFrontMaxT = 4;
 
-__global__ void __launch_bounds__(1024) decode_front_kernel(RouteArgs ra, PlanArgs pa, AssignArgs sa) {
+__global__ void __launch_bounds__(1024) decode_front_kernel(RouteArgs ra, PlanArgs pa, AssignArgs sa,
+                                                           float* __restrict__ zero_buf, size_t zero_n) {
   __shared__ RouteBlockSmem rsm[kFrontMaxT];
   __shared__ int32_t s_counts[256];
   __shared__ int s_tiles[1024];
   __shared__ int s_rows[1024];
   const int tid = threadIdx.x;
   if (tid < 256) s_counts[tid] = 0;
+  for (size_t i = tid; zero_buf && i < zero_n; i += blockDim.x) zero_buf[i] = 0.f;  // the layer's fp32 accumulator
   __syncthreads();
   const int t = tid >> 8;  // this thread's token group
   route_block_body(ra, t, t < ra.T, tid & 255, rsm[t], s_counts);
@@ -553,9 +545,10 @@ bool decode_front_ok(const RouteArgs& ra, const PlanArgs& pa) {
          pa.E_local + (pa.shared_rows > 0 ? 1 : 0) <= 1024;
 }
 
-int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, cudaStream_t s) {
+int launch_decode_front(const RouteArgs& ra, const PlanArgs& pa, const AssignArgs& sa, float* zero_buf, size_t zero_n,
+                        cudaStream_t s) {
   if (!decode_front_ok(ra, pa) || sa.idx_stride > 0 || sa.T_dev) return GEMMS_ERR_SHAPE;
-  decode_front_kernel<<<1, 1024, 0, s>>>(ra, pa, sa);
+  decode_front_kernel<<<1, 1024, 0, s>>>(ra, pa, sa, zero_buf, zero_n);
   GEMMS_CUDA_TRY(cudaGetLastError());
   return GEMMS_OK;
 }
