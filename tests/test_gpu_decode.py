@@ -90,3 +90,20 @@ def test_decode_path_small_geometry_and_residual(decode_limit):
                           rsf=sh.rsf, logits=logits.cpu(), return_fp32=True)
         ref = (ref + res.cpu().float()).to(torch.bfloat16)
         Hh.assert_parity(out, ref, f"decode path c0 T={T} + residual")
+
+
+def test_run_single_token_fp8_input_matches_reference_golden(decode_limit):
+    """run() (FP8 input + given logits) one token at a time: the CUDA-core
+    GEMM1 then reads the e4m3 rows and [H/128, T] scales of the input itself;
+    each row must match the reference's own output for that token."""
+    g = Hh.load_golden()
+    d = {k: v.cuda() for k, v in Hh.golden_weights(g).items() if isinstance(v, torch.Tensor)}
+    T = g["routing_logits"].shape[0]
+    rows = []
+    for t in range(T):
+        rows.append(gemms_b200.run(g["routing_logits"][t:t + 1].contiguous().cuda(), g["routing_bias"].cuda(),
+                                   g["hidden_states"][t:t + 1].contiguous().cuda(),
+                                   g["hidden_states_scale"][:, t:t + 1].contiguous().cuda(), d["w13"],
+                                   d["w13_scale"], d["w2"], d["w2_scale"], 96, 2.5))
+    gemms_b200.check_device_errors(tag="run(T=1)")
+    Hh.assert_parity(torch.cat(rows), Hh.golden_out(g, 96), "run(off=96), each token alone")
