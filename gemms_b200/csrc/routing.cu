@@ -49,6 +49,17 @@ __device__ __forceinline__ float sum_partials_in_order(const float* pp, int n, s
   return x;
 }
 
+// Order-preserving map of fp32 to uint32 (larger float -> larger key) for the
+// warp-wide integer max/min reductions.  The router never compares -0.0 (a
+// sum with a positive sigmoid is never -0), so equal keys are equal floats.
+__device__ __forceinline__ uint32_t f2key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // One warp per token.  Lane l holds experts e = j*32 + l (j < V).
 // Sigmoid: exp is evaluated in double and rounded to fp32 (correctly rounded
 // in practice), then 1/(1+e) and + bias in IEEE fp32 -- the oracle computes
@@ -86,7 +97,39 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
 
   // Group score = sum of the two largest biased scores of the group
   // (flashinfer_baseline.py:108-109).  Groups are aligned lane segments of
-  // width gs within one register j, so a segmented butterfly computes them.
+  // width gs within one register j.
+  bool kept[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) kept[j] = false;
+  if (gs == 32) {
+    float gscore[kMaxV];
+    // One group per register (DeepSeek-V3: 8 groups of 32): the group's
+    // largest key by one warp max, the second by another unless the largest
+    // occurs twice; the group scores are then the same in every lane, and
+    // every lane picks the kept groups in registers, by (score desc, group
+    // asc) as below.
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      gscore[j] = -INFINITY;
+      if (j < V) {
+        const uint32_t k = f2key(sb[j]);
+        const uint32_t m1 = __reduce_max_sync(0xffffffffu, k);
+        uint32_t m2 = m1;
+        if (__popc(__ballot_sync(0xffffffffu, k == m1)) < 2) m2 = __reduce_max_sync(0xffffffffu, k == m1 ? 0u : k);
+        gscore[j] = __fadd_rn(key2f(m1), key2f(m2));
+      }
+    }
+    for (int it = 0; it < a.topk_group; ++it) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < kMaxV; ++j)
+        if (j < V && !kept[j]) argmax_merge(bv, bi, gscore[j], j);
+#pragma unroll
+      for (int j = 0; j < kMaxV; ++j)
+        if (j == bi) kept[j] = true;
+    }
+  } else {
   float gscore[kMaxV];
 #pragma unroll
   for (int j = 0; j < kMaxV; ++j) {
@@ -100,9 +143,6 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
 
   // Keep the topk_group best groups (:112-115).  Group id of (j, lane) is
   // (j*32 + lane) / gs; one lane per group segment proposes its score.
-  bool kept[kMaxV];
-#pragma unroll
-  for (int j = 0; j < kMaxV; ++j) kept[j] = false;
   for (int it = 0; it < a.topk_group; ++it) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -123,6 +163,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       if (j < V && e < E && e / gs == bi) kept[j] = true;
     }
   }
+  }
 
   // Top-k over biased scores of experts in kept groups (:118-120).
   float cand[kMaxV];
@@ -131,9 +172,8 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   int my_e = -1;
   float my_s = 0.f;
   for (int it = 0; it < a.top_k; ++it) {
-    float bv = -INFINITY;
+    float bv = -INFINITY, bs = 0.f;
     int bi = 0x7fffffff;
-    float bs = 0.f;
 #pragma unroll
     for (int j = 0; j < kMaxV; ++j) {
       const int e = j * 32 + lane;
@@ -143,17 +183,15 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
         bs = s[j];
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-        bs = os;
-      }
-    }
+    // warp-wide best (value desc, index asc): the largest key, then the
+    // smallest index among the lanes holding it.  The winner is its owner
+    // lane's own best, so that lane's bs is its unbiased score (0 once no
+    // candidate is left).
+    const uint32_t kb = f2key(bv);
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, kb);
+    bi = static_cast<int>(__reduce_min_sync(0xffffffffu, kb == mk ? static_cast<uint32_t>(bi) : 0x7fffffffu));
+    const float bs_owner = __shfl_sync(0xffffffffu, bs, bi & 31);
+    bs = bi == 0x7fffffff ? 0.f : bs_owner;
     if (lane == it) {
       my_e = bi;
       my_s = bs;
