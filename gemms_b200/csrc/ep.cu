@@ -59,22 +59,37 @@ __device__ __forceinline__ unsigned dest_mask(const int32_t* idx, int top_k, int
   return m;
 }
 
-// Thread per token: per-destination row counts (send_counts[0][d]) and
-// routed (token, expert) pairs (send_counts[1][d]), which size the
-// destination's grouped rows exactly.
-__global__ void ep_count_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k, int E_local, int world,
-                                int32_t* __restrict__ send_counts) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  const int32_t* idx = topk_idx + (size_t)t * top_k;
-  unsigned m = dest_mask(idx, top_k, E_local);
-  while (m) {
-    const int d = __ffs(m) - 1;
-    m &= m - 1;
-    atomicAdd(send_counts + d, 1);
+// Per-destination row counts (send_counts[0][d]) and routed (token, expert)
+// pairs (send_counts[1][d]), which size the destination's grouped rows
+// exactly.  Thread per token; the counts are summed per warp
+// (__reduce_add_sync), then per block in shared memory, and each block adds
+// its 2 x world totals with one global atomic each (per-token atomics onto the
+// same few counters serialise in L2).
+__global__ void __launch_bounds__(256) ep_count_kernel(const int32_t* __restrict__ topk_idx, int T, int top_k,
+                                                       int E_local, int world, int32_t* __restrict__ send_counts) {
+  __shared__ int s_cnt[2 * kMaxWorld];
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid < 2 * world) s_cnt[tid] = 0;
+  __syncthreads();
+  const int stride = gridDim.x * blockDim.x;
+  for (int t0 = blockIdx.x * blockDim.x; t0 < T; t0 += stride) {  // block-uniform trip count
+    const int t = t0 + tid;
+    const int32_t* idx = topk_idx + (size_t)t * top_k;
+    const unsigned m = t < T ? dest_mask(idx, top_k, E_local) : 0u;
+    for (int d = 0; d < world; ++d) {
+      int pairs = 0;
+      if ((m >> d) & 1u)
+        for (int j = 0; j < top_k; ++j) pairs += (idx[j] >= 0 && idx[j] / E_local == d);
+      const unsigned rows_w = __reduce_add_sync(0xffffffffu, (m >> d) & 1u);
+      const unsigned pairs_w = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(pairs));
+      if (lane == 0 && rows_w) {
+        atomicAdd(&s_cnt[d], static_cast<int>(rows_w));
+        atomicAdd(&s_cnt[world + d], static_cast<int>(pairs_w));
+      }
+    }
   }
-  for (int j = 0; j < top_k; ++j)
-    if (idx[j] >= 0) atomicAdd(send_counts + world + idx[j] / E_local, 1);
+  __syncthreads();
+  if (tid < 2 * world && s_cnt[tid]) atomicAdd(send_counts + tid, s_cnt[tid]);
 }
 
 // Block per destination: send rows in increasing token order.
@@ -184,23 +199,40 @@ __global__ void __launch_bounds__(256, 4) ep_pack_kernel(const __nv_bfloat16* __
   }
 }
 
-// Thread per received row: local-expert histogram and pair_row = -1.
-__global__ void ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R, const int32_t* R_dev, int H,
-                               int top_k, int local_offset, int E_local, int32_t* __restrict__ counts,
-                               int32_t* __restrict__ pair_row, int* err) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= R || (R_dev && r >= *R_dev)) return;
-  const int32_t* ids = reinterpret_cast<const int32_t*>(recv + (size_t)r * row_bytes + H + 4 * (H / kBlock));
-  for (int j = 0; j < top_k; ++j) {
-    pair_row[(size_t)r * top_k + j] = -1;
-    const int e = ids[j];
-    if (e < 0) continue;
-    const int le = e - local_offset;
-    if (le >= 0 && le < E_local)
-      atomicAdd(counts + le, 1);
-    else
-      atomicOr(err, kErrBadExpertIndex);
+// Thread per received row (grid-stride): local-expert histogram and
+// pair_row = -1.  Counts go to a per-block histogram in shared memory and each
+// block adds its non-zero bins to `counts` (experts past the shared bins, if
+// E_local ever exceeded them, count with global atomics directly).
+constexpr int kEpHistBins = 1024;
+__global__ void __launch_bounds__(256) ep_hist_kernel(const uint8_t* __restrict__ recv, size_t row_bytes, int R,
+                                                      const int32_t* R_dev, int H, int top_k, int local_offset,
+                                                      int E_local, int32_t* __restrict__ counts,
+                                                      int32_t* __restrict__ pair_row, int* err) {
+  __shared__ int s_hist[kEpHistBins];
+  const int bins = min(E_local, kEpHistBins);
+  for (int i = threadIdx.x; i < bins; i += blockDim.x) s_hist[i] = 0;
+  __syncthreads();
+  const int n = R_dev ? min(R, *R_dev) : R;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
+    const int32_t* ids = reinterpret_cast<const int32_t*>(recv + (size_t)r * row_bytes + H + 4 * (H / kBlock));
+    for (int j = 0; j < top_k; ++j) {
+      pair_row[(size_t)r * top_k + j] = -1;
+      const int e = ids[j];
+      if (e < 0) continue;
+      const int le = e - local_offset;
+      if (le >= 0 && le < E_local) {
+        if (le < bins)
+          atomicAdd(&s_hist[le], 1);
+        else
+          atomicAdd(counts + le, 1);
+      } else {
+        atomicOr(err, kErrBadExpertIndex);
+      }
+    }
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < bins; i += blockDim.x)
+    if (s_hist[i]) atomicAdd(counts + i, s_hist[i]);
 }
 
 // Block per token: out[t] = bf16(acc[t] + sum of the token's returned rows).
@@ -503,7 +535,8 @@ int gemms_ep_dispatch(const int32_t* topk_idx, const float* topk_w, const void* 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);
   GEMMS_CUDA_TRY(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * 2 * world, st));
   if (T == 0) return GEMMS_OK;
-  ep_count_kernel<<<cdiv(T, 256), 256, 0, st>>>(topk_idx, T, top_k, E_local, world, send_counts);
+  ep_count_kernel<<<std::max(1, std::min(cdiv(T, 256), num_sms())), 256, 0, st>>>(topk_idx, T, top_k, E_local,
+                                                                                   world, send_counts);
   GEMMS_CUDA_TRY(cudaGetLastError());
   ep_assign_kernel<<<world, 1024, 0, st>>>(topk_idx, T, top_k, E_local, world, send_counts, send_row_of);
   GEMMS_CUDA_TRY(cudaGetLastError());
@@ -554,8 +587,8 @@ int ep_expert_ffn_impl(const void* recv_buf, int32_t R, const int32_t* R_dev, in
     GEMMS_CUDA_TRY(cudaMemsetAsync(out_rows, 0, sizeof(float) * (size_t)R * H, st));
   }
   int32_t* pair_row = at<int32_t>(ws, L.pair_row);
-  ep_hist_kernel<<<cdiv(R, 256), 256, 0, st>>>(recv, rb, R, R_dev, H, top_k, local_expert_offset, E_local,
-                                                at<int32_t>(ws, L.counts), pair_row, err);
+  ep_hist_kernel<<<std::max(1, std::min(cdiv(R, 256), num_sms())), 256, 0, st>>>(
+      recv, rb, R, R_dev, H, top_k, local_expert_offset, E_local, at<int32_t>(ws, L.counts), pair_row, err);
   GEMMS_CUDA_TRY(cudaGetLastError());
   int rc;
   PlanArgs pa{};
