@@ -123,3 +123,25 @@ def test_router_small_batch_kernel_matches_large_batch_kernel(E, ng, tg, k):
     assert torch.equal(idx_s, idx_l[:48])
     assert torch.equal(w_s, w_l[:48])
     assert torch.equal(c_s.cpu().long(), torch.bincount(idx_s.reshape(-1).cpu().long(), minlength=E))
+
+
+@pytest.mark.parametrize("E,ng,tg,k", [(256, 8, 4, 8), (128, 8, 3, 6), (256, 16, 8, 16)])
+def test_router_exact_ties_same_in_both_kernels(E, ng, tg, k):
+    """Logits on a coarse grid and a zero bias make many experts (and groups)
+    score exactly the same.  Both routers break every tie towards the lower
+    expert (and group) index; the block-per-token router (<= 64 tokens) and
+    the warp-per-token router (larger batches) implement that order
+    differently, so on tied inputs they must still agree bit for bit.  (torch's
+    topk gives no order for ties, so the oracle cannot judge these cases.)"""
+    g = torch.Generator().manual_seed(101 + E + k)
+    logits = (torch.randint(-3, 4, (300, E), generator=g).float() * 0.5).cuda()
+    bias = torch.zeros(E).cuda()
+    idx_l, w_l, c_l = gemms_b200.route(logits, bias, n_group=ng, topk_group=tg, top_k=k, routed_scaling_factor=2.5)
+    idx_s, w_s, _ = gemms_b200.route(logits[:48].contiguous(), bias, n_group=ng, topk_group=tg, top_k=k,
+                                     routed_scaling_factor=2.5)
+    torch.cuda.synchronize()
+    assert torch.equal(idx_s, idx_l[:48])
+    assert torch.equal(w_s, w_l[:48])
+    assert torch.equal(c_l.cpu().long(), torch.bincount(idx_l.reshape(-1).cpu().long(), minlength=E))
+    # every token's k experts are distinct
+    assert all(len(set(row.tolist())) == k for row in idx_l.cpu())
