@@ -50,6 +50,7 @@ EXPORTS = (
     "gemms_moe_fwd_noalloc",
     "gemms_moe_check_noalloc",
     "gemms_test_inject_stall",
+    "gemms_test_workspace_regions",
     "gemms_router_workspace_size",
     "gemms_router_logits",
     "gemms_quantize_1x128",
@@ -194,6 +195,10 @@ def load(auto_build: bool = True) -> ctypes.CDLL:
         L.gemms_moe_check_noalloc.restype = c_int32
         L.gemms_test_inject_stall.argtypes = [c_int32, c_int32, ctypes.c_int64]
         L.gemms_test_inject_stall.restype = c_int32
+        L.gemms_test_workspace_regions.argtypes = [ctypes.POINTER(GemmsMoeShape), ctypes.POINTER(c_size_t),
+                                                   ctypes.POINTER(c_size_t), ctypes.POINTER(c_int32),
+                                                   ctypes.POINTER(c_size_t), ctypes.POINTER(c_size_t)]
+        L.gemms_test_workspace_regions.restype = c_int32
         L.gemms_router_workspace_size.argtypes = [c_int32, c_int32, c_int32]
         L.gemms_router_workspace_size.restype = c_size_t
         L.gemms_router_logits.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,

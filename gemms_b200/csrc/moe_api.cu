@@ -372,6 +372,20 @@ int gemms_moe_fwd(const GemmsMoeArgs* args, void* workspace, size_t ws_bytes, ge
   return GEMMS_OK;
 }
 
+int gemms_test_workspace_regions(const GemmsMoeShape* shape, size_t* rows_off, size_t* scale_off,
+                                  int32_t* scale_ld, size_t* pair_row_off, size_t* offsets_off) {
+  if (!shape || !rows_off || !scale_off || !scale_ld || !pair_row_off || !offsets_off) return GEMMS_ERR_ARG;
+  int rc = check_shape(*shape);
+  if (rc) return rc;
+  const FwdLayout L = fwd_layout(*shape);
+  *rows_off = L.a_rows;
+  *scale_off = L.a_scale;
+  *scale_ld = L.scale_ld;
+  *pair_row_off = L.pair_row;
+  *offsets_off = L.offsets;
+  return GEMMS_OK;
+}
+
 int gemms_moe_check(void* workspace, gemms_stream_t stream_, int32_t* flags) {
   if (!workspace || !flags) return GEMMS_ERR_ARG;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream_);

@@ -351,6 +351,19 @@ int gemms_moe_check_noalloc(gemms_stream_t stream, int32_t* flags);
  * persistent_kernel2.cu:747-757 (no counterpart). */
 int gemms_test_inject_stall(int32_t gemm, int32_t k_iteration, int64_t wait_limit_cycles);
 
+/* Test hook (not for production use): where a gemms_moe_fwd workspace of
+ * this shape keeps, after a call, the layer's expert-grouped activation rows
+ * (e4m3 [R, H], R = T*top_k, + T rows of the shared expert), their fp32
+ * 1x128 scales ([H/128][scale_ld], grouped row fastest), the (token, slot) ->
+ * grouped row map (int32 [T, top_k], -1 for an expert outside the local
+ * range) and the per-group first rows (int32 [E_local + 1 (+1)], the shared
+ * expert's group last), as byte offsets from the workspace base.  Lets a test
+ * compare the rows the permute step wrote with a CPU quantisation.  The
+ * decode path (T at most gemms_set_decode_max_t's limit) writes no grouped
+ * rows.  No counterpart in the reference. */
+int gemms_test_workspace_regions(const GemmsMoeShape* shape, size_t* rows_off, size_t* scale_off,
+                                 int32_t* scale_ld, size_t* pair_row_off, size_t* offsets_off);
+
 /* Static description of an error code. */
 const char* gemms_strerror(int code);
 
