@@ -394,12 +394,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           w12 = __ldg(w1p + kb + 3);
         }
         const int buf = acc_it & 1;
-        // One lane polls the barrier; the warp waits at __syncwarp.
-        int got = 1;
-        if (lane == 0)
-          got = mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err, kErrGemmEpilogueWait, p.wait_limit);
-        got = __shfl_sync(0xffffffffu, got, 0);
-        __syncwarp();
+        // Every lane waits on the barrier itself and the warp agrees with one
+        // vote: no broadcast from a polling lane on this per-K-block path
+        // (lane 0 polling, then a shuffle and __syncwarp, made GEMM1 ~5 %
+        // slower).  The epilogue waits on the MMA, which waits on the
+        // producer, so a lost stage must be reported by the MMA thread and the
+        // epilogue must leave through the abort flag (read every 256 polls).
+        // The single MMA thread's polls sleep up to the suspend hint each, so
+        // its first clock check can come ~256 polls (~0.25 s) into its wait;
+        // the 32 lanes here poll far faster.  Their limit is therefore 4x the
+        // pipeline limit and never under 2^30 cycles (> 0.5 s).
+        const long long epi_limit = p.wait_limit * 4 > (1ll << 30) ? p.wait_limit * 4 : (1ll << 30);
+        const int got = __all_sync(0xffffffffu, mbar_wait(&pfull[buf], (acc_it >> 1) & 1, abort_flag, p.err,
+                                                          kErrGemmEpilogueWait, epi_limit, 1024u));
         if (!got) {
           ok = false;
           break;

@@ -70,17 +70,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with `parity` to complete.  Returns false (after
 // setting *abort and OR-ing `code` into *err) when the wait exceeds
 // `limit_cycles`, or as soon as another role has raised *abort.  The timeout
-// runs on the SM cycle counter (cheap to read), checked every 256 polls;
+// runs on the SM cycle counter (cheap to read); the abort flag is read every
+// 256 polls and the clock every `clock_every` polls (a multiple of 256);
 // reading %globaltimer on every miss added ~1 us to each pipeline hand-off.
+// A suspended poll can last up to the suspend hint, so the first clock check
+// can come long after `limit_cycles`: a role that waits on another role's
+// wait uses a larger `clock_every`, so that the role nearest a lost stage is
+// the one that reports it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code, long long limit_cycles = GEMMS_WAIT_TIMEOUT_CYCLES) {
+                                          int* err, int code, long long limit_cycles = GEMMS_WAIT_TIMEOUT_CYCLES,
+                                          uint32_t clock_every = 256u) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++n & 255u) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > limit_cycles) {
+      if (n % clock_every == 0 && clock64() - t0 > limit_cycles) {
         *abort_flag = 1;
         atomicOr(err, code);
         return false;
