@@ -73,10 +73,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // runs on the SM cycle counter (cheap to read); the abort flag is read every
 // 256 polls and the clock every `clock_every` polls (a multiple of 256);
 // reading %globaltimer on every miss added ~1 us to each pipeline hand-off.
-// A suspended poll can last up to the suspend hint, so the first clock check
-// can come long after `limit_cycles`: a role that waits on another role's
-// wait uses a larger `clock_every`, so that the role nearest a lost stage is
-// the one that reports it.
+// A suspended poll can last up to the suspend hint, so a lone waiting thread's
+// first clock check can come long after `limit_cycles`, while a warp of
+// polling lanes checks far sooner: a role that waits on another role's wait
+// passes a larger limit (and `clock_every`), so that the role nearest a lost
+// stage is the one that reports it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code, long long limit_cycles = GEMMS_WAIT_TIMEOUT_CYCLES,
                                           uint32_t clock_every = 256u) {
