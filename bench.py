@@ -382,12 +382,27 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
     per layer as HBM GB/s; the experts hit are counted from the batch's own
     routing.  For T <= 2 the graph is also timed with the CUDA-core expert
     GEMMs forced on and off (``gemms_set_decode_max_t``), an A/B on one box.  Every step reads >= 396 MB of weights (T=1: 8 experts + shared),
-    more than the 126 MB L2."""
+    more than the 126 MB L2.  Each time is the median of three batches of
+    ``steps`` steps (a decode step is ~0.1 ms: one disturbed batch would
+    otherwise decide the figure)."""
     import torch
 
     import gemms_b200
 
     args = (d["router_w"], d["router_bias"], d["w13"], d["w13_scale"], d["w2"], d["w2_scale"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):  # median over three batches of `steps` calls, ms per call
+        per = []
+        for _ in range(3):
+            e0.record()
+            for _ in range(steps):
+                fn()
+            e1.record()
+            e1.synchronize()
+            per.append(e0.elapsed_time(e1) / steps)
+        return statistics.median(per)
+
     res = {}
     for T in Ts:
         x = d["x"][:T].contiguous()
@@ -396,25 +411,14 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
         for _ in range(warmup):
             gemms_b200.moe(x, *args, **kw)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            gemms_b200.moe(x, *args, **kw)
-        e1.record()
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / steps
+        ms = timed(lambda: gemms_b200.moe(x, *args, **kw))
         # the same layer captured in a CUDA graph (gemms_b200.MoeGraph): one
         # launch per step instead of one per kernel
         graph = gemms_b200.MoeGraph(d, T, **kw)
         for _ in range(warmup):
             graph(x)
         torch.cuda.synchronize()
-        e0.record()
-        for _ in range(steps):
-            graph(x)
-        e1.record()
-        e1.synchronize()
-        ms_g = e0.elapsed_time(e1) / steps
+        ms_g = timed(lambda: graph(x))
         del graph
         ab = {}
         if T <= 2:  # A/B on this box: the graph with the CUDA-core and with the tensor-core expert GEMMs
@@ -426,12 +430,7 @@ def decode_sweep(d, kw, sh, hbm, Ts=(1, 2, 4, 8, 32, 128), steps=50, warmup=5):
                     for _ in range(warmup):
                         graph(x)
                     torch.cuda.synchronize()
-                    e0.record()
-                    for _ in range(steps):
-                        graph(x)
-                    e1.record()
-                    e1.synchronize()
-                    ab[name] = round(e0.elapsed_time(e1) / steps, 5)
+                    ab[name] = round(timed(lambda: graph(x)), 5)
                     del graph
                 finally:
                     L.gemms_set_decode_max_t(prev)
